@@ -1,0 +1,515 @@
+// C ABI of shrimp_b200 (declared in include/shrimp_b200.h): argument checks,
+// workspace layout, kernel launches and the ShrimpNet serve-forward schedule.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/shrimp_b200.h"
+#include "attention.cuh"
+#include "aux.cuh"
+#include "gemm.cuh"
+
+namespace sb {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return SB_OK;
+}
+
+inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
+inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
+
+// N tile for an n-wide GEMM: one tile when n <= 256, else the fewest equal
+// tiles (multiples of 16) of at most 256 columns.
+int choose_bn(int n) {
+  if (n % 16 != 0) return -1;
+  for (int k = 1; k <= 16; ++k) {
+    if (n % k) continue;
+    const int bn = n / k;
+    if (bn <= 256 && bn % 16 == 0) return bn;
+  }
+  return -1;
+}
+
+// Raise a kernel's dynamic shared-memory limit once per (device, kernel).
+int ensure_smem(const void* fn, int bytes) {
+  struct Entry { const void* fn; int dev; int bytes; };
+  static thread_local Entry cache[64];
+  static thread_local int used = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == fn && cache[i].dev == dev && cache[i].bytes >= bytes) return SB_OK;
+  const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, "shared-memory attribute: %s", cudaGetErrorString(e));
+  if (used < 64) cache[used++] = Entry{fn, dev, bytes};
+  return SB_OK;
+}
+
+template <typename T, int STAGES>
+int launch_gemm_stages(const GemmArgs& a, cudaStream_t st) {
+  const int smem = gemm_smem_bytes(a.bn, STAGES);
+  if (int s = ensure_smem(reinterpret_cast<const void*>(gemm_tc_kernel<T, STAGES>), smem)) return s;
+  dim3 grid((unsigned)cdiv(a.M, kBlockM), (unsigned)(a.n_total / a.bn));
+  gemm_tc_kernel<T, STAGES><<<grid, kGemmThreads, smem, st>>>(a);
+  return check_launch("gemm_tc_kernel");
+}
+
+template <typename T>
+int launch_gemm(GemmArgs a, cudaStream_t st) {
+  if (a.M <= 0) return SB_OK;
+  if (a.bn <= 0) a.bn = choose_bn(a.n_total);
+  if (a.bn <= 0 || a.bn > 256 || a.bn % 16 || a.n_total % a.bn)
+    return fail(SB_ERR_UNSUPPORTED, "gemm: N=%d cannot be tiled (need a multiple of 16)", a.n_total);
+  if (a.kpad % kChunkK || a.kpad < a.taps * a.cin)
+    return fail(SB_ERR_INVALID_ARG, "gemm: kpad=%d must be a multiple of 64 covering taps*cin=%d", a.kpad,
+                a.taps * a.cin);
+  if (a.cin % 8) return fail(SB_ERR_UNSUPPORTED, "gemm: input channels per tap (%d) must be a multiple of 8", a.cin);
+  if ((a.flags & (EPI_LN_A | EPI_LN_B | EPI_HEAD)) && a.bn != a.n_total)
+    return fail(SB_ERR_UNSUPPORTED, "gemm: row-wise epilogue needs N=%d <= 256", a.n_total);
+  if (a.bn <= 128) return launch_gemm_stages<T, 6>(a, st);
+  return launch_gemm_stages<T, 4>(a, st);
+}
+
+template <typename T>
+int launch_attention(const AttnArgs& a, cudaStream_t st) {
+  if (a.D % 8 || a.D <= 0 || a.D > 64)
+    return fail(SB_ERR_UNSUPPORTED, "attention: head_dim=%d must be a multiple of 8 in [8, 64]", a.D);
+  if (a.table_rows > kMaxTableRows) return fail(SB_ERR_UNSUPPORTED, "attention: %d bias rows > %d", a.table_rows, kMaxTableRows);
+  dim3 grid((unsigned)cdiv(a.S, kAttnBlockQ), (unsigned)a.H, (unsigned)a.B);
+  const int dp = round_up(a.D, 16);
+#define SB_ATTN_CASE(DPV)                                                                 \
+  case DPV: {                                                                             \
+    const int smem = AttnSmem<DPV>::kBytes;                                               \
+    if (int s = ensure_smem(reinterpret_cast<const void*>(attn_kernel<T, DPV>), smem)) return s; \
+    attn_kernel<T, DPV><<<grid, kAttnThreads, smem, st>>>(a);                            \
+    return check_launch("attn_kernel");                                                   \
+  }
+  switch (dp) {
+    SB_ATTN_CASE(16)
+    SB_ATTN_CASE(32)
+    SB_ATTN_CASE(48)
+    SB_ATTN_CASE(64)
+    default: break;
+  }
+#undef SB_ATTN_CASE
+  return fail(SB_ERR_UNSUPPORTED, "attention: head_dim=%d", a.D);
+}
+
+// ---- forward workspace --------------------------------------------------------
+
+struct FwdLayout {
+  size_t seq32, lnf32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, total;
+};
+
+FwdLayout fwd_layout(int C, int B, int npad) {
+  const size_t S = (size_t)npad + kNumTok;
+  const size_t R = (size_t)B * S;
+  const size_t Mc = (size_t)B * npad;
+  FwdLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  L.seq32 = take(R * C * 4);
+  L.lnf32 = take(R * C * 4);
+  L.xa16 = take(R * C * 2);
+  L.y16 = take(R * C * 2);
+  L.qkv16 = take(R * 3 * C * 2);
+  L.o16 = take(R * C * 2);
+  L.u16 = take(R * 2 * C * 2);
+  L.feat16 = take(R * kFeatPad * 2);
+  L.gidx = take(Mc * 7 * 4);
+  L.rowmask = take(R * 4);
+  L.coords32 = take(Mc * 2 * 4);
+  L.total = off;
+  return L;
+}
+
+int validate_net(const sb_net* net) {
+  if (!net) return fail(SB_ERR_INVALID_ARG, "net is NULL");
+  const int C = net->channels, H = net->heads;
+  if (C <= 0 || C > 256 || C % 32) return fail(SB_ERR_UNSUPPORTED, "channels=%d: need a multiple of 32 <= 256", C);
+  if (H <= 0 || C % H) return fail(SB_ERR_INVALID_ARG, "channels=%d not divisible by heads=%d", C, H);
+  const int D = C / H;
+  if (D % 8 || D > 64) return fail(SB_ERR_UNSUPPORTED, "head_dim=%d: need a multiple of 8 <= 64", D);
+  const int nb = net->num_blocks;
+  if (nb <= 0 || nb > SB_MAX_BLOCKS || (int)strnlen(net->layout, SB_MAX_BLOCKS + 1) != nb)
+    return fail(SB_ERR_INVALID_ARG, "layout length %d invalid", nb);
+  if (net->layout[nb - 1] != 'A') return fail(SB_ERR_INVALID_ARG, "layout must end with 'A'");
+  for (int i = 0; i < nb; ++i)
+    if (net->layout[i] != 'A' && net->layout[i] != 'C') return fail(SB_ERR_INVALID_ARG, "layout char %d", i);
+  return SB_OK;
+}
+
+}  // namespace
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" {
+
+int sb_abi_version(void) { return SB_ABI_VERSION; }
+
+int sb_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return SB_ERR_INVALID_ARG;
+  snprintf(buf, len, "%s", g_last_error.c_str());
+  return SB_OK;
+}
+
+int sb_forward_workspace_bytes(const sb_net* net, int batch, int npad, size_t* bytes) {
+  if (int s = validate_net(net)) return s;
+  if (!bytes || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "workspace query: bad batch/npad");
+  *bytes = fwd_layout(net->channels, batch, npad).total;
+  return SB_OK;
+}
+
+int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* out, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (int s = validate_net(net)) return s;
+  if (!in || !out || !out->policy || !out->value_logits) return fail(SB_ERR_INVALID_ARG, "inputs/outputs missing");
+  const int B = in->batch, npad = in->npad, C = net->channels, H = net->heads;
+  if (B == 0) return SB_OK;
+  if (B < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "batch=%d npad=%d", B, npad);
+  if (!in->feats || !in->nbr || !in->mask || !in->coords) return fail(SB_ERR_INVALID_ARG, "input pointer NULL");
+  const FwdLayout L = fwd_layout(C, B, npad);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SB_ERR_WORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, L.total);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  float* seq32 = reinterpret_cast<float*>(ws + L.seq32);
+  float* lnf32 = reinterpret_cast<float*>(ws + L.lnf32);
+  __half* xa16 = reinterpret_cast<__half*>(ws + L.xa16);
+  __half* y16 = reinterpret_cast<__half*>(ws + L.y16);
+  __half* qkv16 = reinterpret_cast<__half*>(ws + L.qkv16);
+  __half* o16 = reinterpret_cast<__half*>(ws + L.o16);
+  __half* u16 = reinterpret_cast<__half*>(ws + L.u16);
+  __half* feat16 = reinterpret_cast<__half*>(ws + L.feat16);
+  int32_t* gidx = reinterpret_cast<int32_t*>(ws + L.gidx);
+  float* rowmask = reinterpret_cast<float*>(ws + L.rowmask);
+  int32_t* coords32 = reinterpret_cast<int32_t*>(ws + L.coords32);
+  int* err = out->status;
+
+  const int S = npad + kNumTok;
+  const long long R = (long long)B * S;
+  const long long Mc = (long long)B * npad;
+  if (R > (1LL << 31) - 1) return fail(SB_ERR_UNSUPPORTED, "batch too large");
+  const int D = C / H;
+  const float eps = 1e-5f;
+
+  {
+    PrepArgs p{};
+    p.feats = in->feats; p.feats_dtype = in->feats_dtype;
+    p.nbr = in->nbr; p.nbr_dtype = in->nbr_dtype;
+    p.mask = in->mask; p.mask_dtype = in->mask_dtype;
+    p.coords = in->coords; p.coords_dtype = in->coords_dtype;
+    p.B = B; p.npad = npad; p.S = S;
+    p.feat16 = feat16; p.gidx = gidx; p.rowmask = rowmask; p.coords32 = coords32; p.err = err;
+    const long long work = Mc > (long long)B * kNumTok ? Mc : (long long)B * kNumTok;
+    prep_cells_kernel<<<(unsigned)cdiv(work, 256), 256, 0, st>>>(p);
+    if (int s = check_launch("prep_cells_kernel")) return s;
+    const long long tot = (long long)B * kNumTok * C;
+    init_tokens_kernel<<<(unsigned)cdiv(tot, 256), 256, 0, st>>>(net->tokens, (const __half*)net->tokens_ln16, B, S,
+                                                                   C, seq32, xa16);
+    if (int s = check_launch("init_tokens_kernel")) return s;
+  }
+
+  const int nb = net->num_blocks;
+  int first_attn = -1;
+  for (int i = 0; i < nb; ++i)
+    if (net->layout[i] == 'A') { first_attn = i; break; }
+  // attention block index of the first 'A' at or after position i
+  auto next_attn_index = [&](int pos) {
+    int ai = 0;
+    for (int i = 0; i < pos; ++i) ai += net->layout[i] == 'A';
+    return ai;
+  };
+
+  auto conv_args = [&](const void* x, const void* w, const float* bias) {
+    GemmArgs g{};
+    g.A = x; g.lda = C; g.cin = C; g.taps = 7; g.gidx = gidx; g.M = (int)Mc;
+    g.Bw = w; g.kpad = round_up(7 * C, kChunkK); g.n_total = C; g.bn = C;
+    g.bias = bias; g.eps = eps; g.rowmask = rowmask; g.seq_len = S; g.ntok = kNumTok; g.err = err;
+    return g;
+  };
+  auto linear_args = [&](const void* x, int k, const void* w, int n, const float* bias) {
+    GemmArgs g{};
+    g.A = x; g.lda = k; g.cin = k; g.taps = 1; g.gidx = nullptr; g.M = (int)R;
+    g.Bw = w; g.kpad = round_up(k, kChunkK); g.n_total = n; g.bn = 0;
+    g.bias = bias; g.eps = eps; g.rowmask = rowmask; g.seq_len = S; g.ntok = kNumTok; g.err = err;
+    return g;
+  };
+
+  // stem: relu(LN(conv(feats))) * mask (model.py:865)
+  {
+    GemmArgs g = conv_args(feat16, net->stem_w, net->stem_b);
+    g.lda = kFeatPad; g.cin = kFeatPad; g.kpad = round_up(7 * kFeatPad, kChunkK);
+    g.ln_a_w = net->stem_ln_w; g.ln_a_b = net->stem_ln_b;
+    g.flags = EPI_LN_A | EPI_RELU | EPI_MASK | EPI_OUT32 | EPI_OUT16;
+    g.out32 = seq32; g.ld32 = C; g.out16 = xa16; g.ld16 = C;
+    if (first_attn == 0) {
+      g.flags |= EPI_LN_B;
+      g.ln_b_w = net->attn[0].ln1_w; g.ln_b_b = net->attn[0].ln1_b;
+    }
+    if (int s = launch_gemm<__half>(g, st)) return s;
+  }
+
+  int ci = 0, ai = 0;
+  for (int pos = 0; pos < nb; ++pos) {
+    const bool next_is_attn = pos + 1 < nb && net->layout[pos + 1] == 'A';
+    if (net->layout[pos] == 'C') {
+      const sb_conv_block_weights& w = net->conv[ci++];
+      GemmArgs g1 = conv_args(xa16, w.w1, w.b1);
+      g1.ln_a_w = w.ln1_w; g1.ln_a_b = w.ln1_b;
+      g1.flags = EPI_LN_A | EPI_RELU | EPI_MASK | EPI_OUT16;
+      g1.out16 = y16; g1.ld16 = C;
+      if (int s = launch_gemm<__half>(g1, st)) return s;
+      GemmArgs g2 = conv_args(y16, w.w2, w.b2);
+      g2.ln_a_w = w.ln2_w; g2.ln_a_b = w.ln2_b; g2.gamma = w.gamma;
+      g2.flags = EPI_LN_A | EPI_MASK | EPI_RESID | EPI_POST_RELU | EPI_OUT32 | EPI_OUT16;
+      g2.out32 = seq32; g2.ld32 = C; g2.out16 = xa16; g2.ld16 = C;
+      if (next_is_attn) {
+        const int na = next_attn_index(pos + 1);
+        g2.flags |= EPI_LN_B;
+        g2.ln_b_w = net->attn[na].ln1_w; g2.ln_b_b = net->attn[na].ln1_b;
+      }
+      if (int s = launch_gemm<__half>(g2, st)) return s;
+    } else {
+      const sb_attn_block_weights& w = net->attn[ai];
+      // q | k | v projections of LN1(seq) (model.py:448-455)
+      GemmArgs gq = linear_args(xa16, C, w.wqkv, 3 * C, w.bqkv);
+      gq.flags = EPI_OUT16; gq.out16 = qkv16; gq.ld16 = 3 * C;
+      if (int s = launch_gemm<__half>(gq, st)) return s;
+      // biased attention core
+      AttnArgs at{};
+      at.q = qkv16; at.k = qkv16 + C; at.v = qkv16 + 2 * C;
+      at.pos_stride = (long long)S * 3 * C; at.row_stride = 3 * C; at.head_stride = D;
+      at.out = o16; at.out_pos_stride = (long long)S * C; at.out_row_stride = C; at.out_head_stride = D;
+      at.B = B; at.S = S; at.H = H; at.D = D; at.ntok = kNumTok;
+      at.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+      at.mode = BIAS_COORDS; at.table = w.bias_table; at.table_rows = SB_BIAS_ROWS + 1;
+      at.coords = coords32; at.keymask = rowmask; at.lut = net->lut;
+      if (int s = launch_attention<__half>(at, st)) return s;
+      // out_proj, gamma * mask residual; LN2 for the MLP (model.py:511-512)
+      GemmArgs go = linear_args(o16, C, w.wo, C, w.bo);
+      go.flags = EPI_MASK | EPI_RESID | EPI_OUT32 | EPI_OUT16 | EPI_LN_B;
+      go.gamma = w.gamma_attn; go.out32 = seq32; go.ld32 = C; go.out16 = y16; go.ld16 = C;
+      go.ln_b_w = w.ln2_w; go.ln_b_b = w.ln2_b;
+      if (int s = launch_gemm<__half>(go, st)) return s;
+      // fc1 + GELU
+      GemmArgs gf1 = linear_args(y16, C, w.w1, 2 * C, w.b1);
+      gf1.flags = EPI_GELU | EPI_OUT16; gf1.out16 = u16; gf1.ld16 = 2 * C;
+      if (int s = launch_gemm<__half>(gf1, st)) return s;
+      // fc2, gamma * mask residual; LN for whatever reads the stream next
+      GemmArgs gf2 = linear_args(u16, 2 * C, w.w2, C, w.b2);
+      gf2.flags = EPI_MASK | EPI_RESID | EPI_OUT32 | EPI_OUT16 | EPI_LN_B;
+      gf2.gamma = w.gamma_mlp; gf2.out32 = seq32; gf2.ld32 = C; gf2.out16 = xa16; gf2.ld16 = C;
+      if (pos == nb - 1) {
+        gf2.ln_b_w = net->ln_final_w; gf2.ln_b_b = net->ln_final_b;
+        gf2.flags |= EPI_OUT32B; gf2.out32b = lnf32; gf2.ld32b = C;
+      } else {
+        const int na = ai + 1;
+        gf2.ln_b_w = net->attn[na].ln1_w; gf2.ln_b_b = net->attn[na].ln1_b;
+        if (!next_is_attn) gf2.flags |= EPI_LNB_TOKENS;
+      }
+      if (int s = launch_gemm<__half>(gf2, st)) return s;
+      ++ai;
+    }
+  }
+
+  // policy: (relu(conv(cells)) . w + b) * mask (model.py:1011-1020)
+  {
+    GemmArgs g = conv_args(xa16, net->policy_conv_w, net->policy_conv_b);
+    g.flags = EPI_HEAD; g.head_w = net->policy_head_w; g.head_b = net->policy_head_b; g.head_out = out->policy;
+    if (int s = launch_gemm<__half>(g, st)) return s;
+  }
+  // value (+ moves-left) heads and decode (model.py:984-1003, losses.py:40-61)
+  {
+    HeadsArgs h{};
+    h.lnf32 = lnf32; h.rowmask = rowmask; h.B = B; h.S = S; h.C = C;
+    h.vr_wT = net->value_red_wT; h.vr_b = net->value_red_b; h.vh_wT = net->value_head_wT; h.vh_b = net->value_head_b;
+    h.value_logits = out->value_logits; h.value = out->value;
+    if (out->ml_logits) {
+      h.mr_wT = net->ml_red_wT; h.mr_b = net->ml_red_b; h.mh_wT = net->ml_head_wT; h.mh_b = net->ml_head_b;
+      h.ml_logits = out->ml_logits; h.ml = out->moves_left;
+    }
+    const int smem = (kHeadsPos * 3 * C + kHeadsPos * C + kHeadsPos * kBins + kHeadsPos) * 4;
+    if (int s = ensure_smem(reinterpret_cast<const void*>(heads_kernel), smem)) return s;
+    heads_kernel<<<(unsigned)cdiv(B, kHeadsPos), kHeadsThreads, smem, st>>>(h);
+    if (int s = check_launch("heads_kernel")) return s;
+  }
+  return SB_OK;
+}
+
+int sb_build_gather_index(const void* nbr, int nbr_dtype, int batch, int npad, int32_t* out, int32_t* status,
+                          void* stream) {
+  if (!nbr || !out || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "gather index: bad args");
+  const long long n = (long long)batch * npad;
+  if (n == 0) return SB_OK;
+  gather_index_kernel<<<(unsigned)cdiv(n, 256), 256, 0, (cudaStream_t)stream>>>(nbr, nbr_dtype, batch, npad, out,
+                                                                                 status);
+  return check_launch("gather_index_kernel");
+}
+
+int sb_build_pair_u8(const void* coords, int coords_dtype, const void* mask, int mask_dtype, int batch, int npad,
+                     const uint8_t* lut, uint8_t* out, void* stream) {
+  if (!coords || !mask || !lut || !out || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "pair: bad args");
+  const long long S = npad + kNumTok;
+  const long long n = (long long)batch * S * S;
+  if (n == 0) return SB_OK;
+  pair_u8_kernel<<<(unsigned)cdiv(n, 256), 256, 0, (cudaStream_t)stream>>>(coords, coords_dtype, mask, mask_dtype,
+                                                                            batch, npad, lut, out);
+  return check_launch("pair_u8_kernel");
+}
+
+int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes) {
+  if (!bytes || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "hex_conv workspace: bad args");
+  const size_t rows = (size_t)batch * npad;
+  *bytes = ((rows * 7 * 4 + 255) & ~size_t(255)) + rows * 4;
+  return SB_OK;
+}
+
+static int hex_conv_common(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w,
+                           const float* bias, const float* ln_w, const float* ln_b, float eps, int flags,
+                           int batch, int npad, int cin, int cout, void* out, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!x || !gather_idx || !mask || !w || !bias || !out || batch < 0 || npad <= 0)
+    return fail(SB_ERR_INVALID_ARG, "hex_conv: bad args");
+  size_t need = 0;
+  sb_hex_conv_workspace_bytes(batch, npad, &need);
+  if (!workspace || workspace_bytes < need) return fail(SB_ERR_WORKSPACE, "hex_conv: workspace too small");
+  const long long rows = (long long)batch * npad;
+  if (rows == 0) return SB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  int32_t* gabs = reinterpret_cast<int32_t*>(workspace);
+  float* rm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + ((rows * 7 * 4 + 255) & ~255LL));
+  absolute_gidx_kernel<<<(unsigned)cdiv(rows * 7, 256), 256, 0, st>>>(gather_idx, batch, npad, 7, gabs);
+  if (int s = check_launch("absolute_gidx_kernel")) return s;
+  mask_to_float_kernel<<<(unsigned)cdiv(rows, 256), 256, 0, st>>>(mask, rows, rm);
+  if (int s = check_launch("mask_to_float_kernel")) return s;
+  GemmArgs g{};
+  g.A = x; g.lda = cin; g.cin = cin; g.taps = 7; g.gidx = gabs; g.M = (int)rows;
+  g.Bw = w; g.kpad = round_up(7 * cin, kChunkK); g.n_total = cout; g.bn = 0;
+  g.bias = bias; g.ln_a_w = ln_w; g.ln_a_b = ln_b; g.eps = eps; g.rowmask = rm;
+  g.flags = flags | EPI_MASK | EPI_OUT16; g.out16 = out; g.ld16 = cout;
+  return launch_gemm<__half>(g, st);
+}
+
+int sb_hex_conv(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w, const float* bias,
+                int batch, int npad, int cin, int cout, void* out, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  return hex_conv_common(x, gather_idx, mask, w, bias, nullptr, nullptr, 0.f, 0, batch, npad, cin, cout, out,
+                         workspace, workspace_bytes, stream);
+}
+
+int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w, const float* bias,
+                   const float* ln_w, const float* ln_b, float eps, int relu, int batch, int npad, int cin, int cout,
+                   void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ln_w || !ln_b) return fail(SB_ERR_INVALID_ARG, "hex_conv_ln: LayerNorm params NULL");
+  return hex_conv_common(x, gather_idx, mask, w, bias, ln_w, ln_b, eps, EPI_LN_A | (relu ? EPI_RELU : 0), batch,
+                         npad, cin, cout, out, workspace, workspace_bytes, stream);
+}
+
+int sb_attn_pair(const void* q, const void* k, const void* v, const uint8_t* pair, const float* table2, int batch,
+                 int heads, int seq, int head_dim, void* out, void* stream) {
+  if (!q || !k || !v || !pair || !table2 || !out || batch < 0 || heads <= 0 || seq <= 0)
+    return fail(SB_ERR_INVALID_ARG, "attn_pair: bad args");
+  if (batch == 0) return SB_OK;
+  AttnArgs a{};
+  a.q = q; a.k = k; a.v = v;
+  a.pos_stride = (long long)heads * seq * head_dim; a.head_stride = (long long)seq * head_dim; a.row_stride = head_dim;
+  a.out = out; a.out_pos_stride = a.pos_stride; a.out_head_stride = a.head_stride; a.out_row_stride = head_dim;
+  a.B = batch; a.S = seq; a.H = heads; a.D = head_dim; a.ntok = 0;
+  a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  a.mode = BIAS_PAIR; a.table = table2; a.table_rows = SB_BIAS_ROWS + 1; a.pair = pair;
+  return launch_attention<__half>(a, (cudaStream_t)stream);
+}
+
+int sb_pack_hex_conv_weight(const float* w, int taps, int cin, int cin_pad, int cout, void* out, void* stream) {
+  if (!w || !out || taps <= 0 || cin <= 0 || cin_pad < cin || cout <= 0) return fail(SB_ERR_INVALID_ARG, "pack conv");
+  const int kpad = round_up(taps * cin_pad, kChunkK);
+  const long long n = (long long)cout * kpad;
+  pack_conv_kernel<<<(unsigned)cdiv(n, 256), 256, 0, (cudaStream_t)stream>>>(w, taps, cin, cin_pad, cout, kpad,
+                                                                              (__half*)out);
+  return check_launch("pack_conv_kernel");
+}
+
+int sb_pack_linear_weight(const float* w, int n, int k, void* out, void* stream) {
+  if (!w || !out || n <= 0 || k <= 0) return fail(SB_ERR_INVALID_ARG, "pack linear");
+  const int kpad = round_up(k, kChunkK);
+  const long long tot = (long long)n * kpad;
+  pack_linear_kernel<<<(unsigned)cdiv(tot, 256), 256, 0, (cudaStream_t)stream>>>(w, n, k, kpad, (__half*)out);
+  return check_launch("pack_linear_kernel");
+}
+
+int sb_decode_binned(const float* logits, int batch, float scale, float offset, float* out, void* stream) {
+  if (!logits || !out || batch < 0) return fail(SB_ERR_INVALID_ARG, "decode: bad args");
+  if (batch == 0) return SB_OK;
+  decode_binned_kernel<<<(unsigned)cdiv(batch, 128), 128, 0, (cudaStream_t)stream>>>(logits, batch, scale, offset,
+                                                                                      out);
+  return check_launch("decode_binned_kernel");
+}
+
+int sb_legal_prefix_softmax(const float* policy, int batch, int npad, const int32_t* legal, const int64_t* offs,
+                            float* out, void* stream) {
+  if (!policy || !legal || !offs || !out || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "softmax: bad args");
+  if (batch == 0) return SB_OK;
+  legal_softmax_kernel<<<(unsigned)cdiv((long long)batch * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+      policy, batch, npad, legal, offs, out);
+  return check_launch("legal_softmax_kernel");
+}
+
+int sb_raytap_conv(const void* x, const int32_t* nbr, int taps, const void* w, const float* bias, int batch, int n,
+                   int c, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !nbr || !w || !bias || !out || batch < 0 || n <= 0 || taps <= 0) return fail(SB_ERR_INVALID_ARG, "raytap: bad args");
+  const size_t need = (size_t)batch * n * taps * 4;
+  if (!workspace || workspace_bytes < need) return fail(SB_ERR_WORKSPACE, "raytap: workspace < %zu", need);
+  if (batch == 0) return SB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  int32_t* g = reinterpret_cast<int32_t*>(workspace);
+  shared_gidx_kernel<<<(unsigned)cdiv((long long)batch * n * taps, 256), 256, 0, st>>>(nbr, batch, n, taps, g);
+  if (int s = check_launch("shared_gidx_kernel")) return s;
+  GemmArgs a{};
+  a.A = x; a.lda = c; a.cin = c; a.taps = taps; a.gidx = g; a.M = batch * n;
+  a.Bw = w; a.kpad = round_up(taps * c, kChunkK); a.n_total = c; a.bn = 0;
+  a.bias = bias; a.flags = EPI_RES16 | EPI_OUT16; a.res16 = x; a.ldr16 = c; a.out16 = out; a.ld16 = c;
+  return launch_gemm<__nv_bfloat16>(a, st);
+}
+
+int sb_offset_attention(const void* q, const void* k, const void* v, const float* table, int table_rows,
+                        const int32_t* offset_map, int batch, int len, int heads, int head_dim, void* out,
+                        void* stream) {
+  if (!q || !k || !v || !table || !offset_map || !out || batch < 0 || len <= 0 || heads <= 0)
+    return fail(SB_ERR_INVALID_ARG, "offset attention: bad args");
+  if (batch == 0) return SB_OK;
+  AttnArgs a{};
+  a.q = q; a.k = k; a.v = v;
+  a.pos_stride = (long long)len * heads * head_dim; a.row_stride = (long long)heads * head_dim; a.head_stride = head_dim;
+  a.out = out; a.out_pos_stride = a.pos_stride; a.out_row_stride = a.row_stride; a.out_head_stride = head_dim;
+  a.B = batch; a.S = len; a.H = heads; a.D = head_dim; a.ntok = 0;
+  a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  a.mode = BIAS_OFFSET; a.table = table; a.table_rows = table_rows; a.offset_map = offset_map;
+  return launch_attention<__nv_bfloat16>(a, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,195 @@
+/*
+ * shrimp_b200 — C ABI of the B200-native Shrimp leaf-evaluation forward.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), enqueues its kernels on that stream without any host
+ * synchronisation, and returns an sb_status. No exceptions cross the ABI and no
+ * kernel traps: a device-side fault condition (out-of-range neighbour index, a
+ * bounded wait that gave up) sets bits in the caller's status word instead.
+ * The caller owns every buffer (inputs, outputs, weights, workspace); the
+ * library never allocates or frees device memory.
+ *
+ * Conventions
+ *   - "f16 rows": row-major IEEE half matrices; weights of the tensor-core
+ *     layers are packed K-major as [N][Kpad] halves with Kpad a multiple of 64
+ *     (see sb_pack_hex_conv_weight / sb_pack_linear_weight).
+ *   - Sequence layout: every position owns S = 8 + Npad consecutive rows, the 8
+ *     summary tokens first, then its Npad cells (reference model.py:905-926).
+ *   - dtype codes: SB_F32, SB_F16, SB_BF16, SB_I64, SB_I32, SB_U8 (also bool),
+ *     SB_I16, SB_U16.
+ *
+ * Reference interfaces replaced (paths inside Cmiller132/hexo-bot):
+ *   packages/shrimp/python/shrimp/model.py            ShrimpNet and its blocks
+ *   packages/shrimp/python/shrimp/_triton_conv.py     shrimp::hex_conv, shrimp::hex_conv_ln
+ *   packages/shrimp/python/shrimp/_triton_attn.py     shrimp::attn_pair
+ *   packages/shrimp/python/shrimp/losses.py           decode_binned_value / decode_moves_left
+ *   packages/shrimp/python/shrimp/inference.py        ShrimpEvaluator._decode_group
+ */
+#ifndef SHRIMP_B200_H_
+#define SHRIMP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_ABI_VERSION 1
+#define SB_MAX_BLOCKS 32
+#define SB_NUM_TOKENS 8
+#define SB_NUM_FEATURES 15
+#define SB_VALUE_BINS 65
+#define SB_BIAS_ROWS 237      /* learned rows; row 237 is the pad-key row */
+#define SB_LUT_W 35           /* clamped-offset LUT is SB_LUT_W x SB_LUT_W */
+
+typedef enum {
+  SB_OK = 0,
+  SB_ERR_INVALID_ARG = 1,
+  SB_ERR_UNSUPPORTED = 2,
+  SB_ERR_CUDA = 3,
+  SB_ERR_WORKSPACE = 4
+} sb_status;
+
+typedef enum {
+  SB_F32 = 0,
+  SB_F16 = 1,
+  SB_BF16 = 2,
+  SB_I64 = 3,
+  SB_I32 = 4,
+  SB_U8 = 5,
+  SB_I16 = 6,
+  SB_U16 = 7
+} sb_dtype;
+
+/* Status-word bits written by kernels (caller-provided int32 on the device). */
+#define SB_DEV_ERR_TIMEOUT 1    /* a bounded mbarrier wait gave up */
+#define SB_DEV_ERR_NBR_RANGE 2  /* a neighbour index was > Npad (treated as missing) */
+
+/* ---- weights ----------------------------------------------------------------
+ * Device pointers into caller-owned packed weights. "hw" = f16 [N][Kpad]
+ * K-major; everything else fp32. */
+typedef struct {
+  const void* w1;  const float* b1;  const float* ln1_w; const float* ln1_b;
+  const void* w2;  const float* b2;  const float* ln2_w; const float* ln2_b;
+  const float* gamma;                 /* ls.gamma */
+} sb_conv_block_weights;               /* ConvBlock, model.py:384-422 */
+
+typedef struct {
+  const float* ln1_w; const float* ln1_b;
+  const void* wqkv;  const float* bqkv; /* [3C][C] = q_proj; k_proj; v_proj */
+  const void* wo;    const float* bo;
+  const float* gamma_attn;
+  const float* ln2_w; const float* ln2_b;
+  const void* w1;    const float* b1;   /* fc1 [2C][C] */
+  const void* w2;    const float* b2;   /* fc2 [C][2C] */
+  const float* gamma_mlp;
+  const float* bias_table;              /* [238][H]: rows 0..236 = table rounded to f16, row 237 = -3e4 */
+} sb_attn_block_weights;               /* AttnBlock, model.py:497-514 */
+
+typedef struct {
+  int channels;
+  int heads;
+  int num_blocks;
+  char layout[SB_MAX_BLOCKS + 1];       /* 'C' / 'A', ends with 'A' */
+  const void* stem_w;  const float* stem_b;   /* stem: Kpad over 7 taps x 16 (15 features + 0) */
+  const float* stem_ln_w; const float* stem_ln_b;
+  const float* tokens;                  /* [8][C] */
+  const void* tokens_ln16;              /* [8][C] f16 = LN1 of the first attention block applied to tokens */
+  const float* ln_final_w; const float* ln_final_b;
+  const void* policy_conv_w; const float* policy_conv_b;
+  const float* policy_head_w; float policy_head_b;
+  const float* value_red_wT; const float* value_red_b;   /* [3C][C], [C] */
+  const float* value_head_wT; const float* value_head_b; /* [C][65], [65] */
+  const float* ml_red_wT; const float* ml_red_b;
+  const float* ml_head_wT; const float* ml_head_b;
+  const uint8_t* lut;                   /* [35*35] clamped-offset -> bias row */
+  sb_conv_block_weights conv[SB_MAX_BLOCKS];
+  sb_attn_block_weights attn[SB_MAX_BLOCKS];
+} sb_net;
+
+typedef struct {
+  const void* feats;  int feats_dtype;  /* (B, Npad, 15) f32 / f16 / bf16 */
+  const void* nbr;    int nbr_dtype;    /* (B, Npad, 6) i64 / i32 / u16; missing = Npad, -1 or 0xFFFF */
+  const void* mask;   int mask_dtype;   /* (B, Npad) bool / u8 */
+  const void* coords; int coords_dtype; /* (B, Npad, 2) i64 / i32 / i16 */
+  int batch;
+  int npad;
+} sb_inputs;
+
+typedef struct {
+  float* policy;        /* (B, Npad) logits, pad rows 0 */
+  float* value_logits;  /* (B, 65) */
+  float* value;         /* (B) decoded scalar, or NULL */
+  float* ml_logits;     /* (B, 65) moves-left logits, or NULL (not requested) */
+  float* moves_left;    /* (B) decoded moves-left, or NULL */
+  int32_t* status;      /* device status word (SB_DEV_ERR_* bits), or NULL */
+} sb_outputs;
+
+/* ---- library ------------------------------------------------------------- */
+int sb_abi_version(void);
+/* Copies the last host-side error message of the calling thread. */
+int sb_last_error(char* buf, size_t len);
+
+/* ---- whole forward: ShrimpNet.forward_policy_value (model.py:972-1003) ---- */
+/* Bytes of workspace sb_forward_policy_value needs for (B, Npad). */
+int sb_forward_workspace_bytes(const sb_net* net, int batch, int npad, size_t* bytes);
+int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* out, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* ---- index tables (model.py:860-863 gather_idx; model.py:762-792 _build_pair_u8) */
+/* gather_idx_out (B, Npad, 7) int32 row-local: tap 0 = self, taps 1..6 = nbr,
+ * missing -> Npad (the reference's convention). */
+int sb_build_gather_index(const void* nbr, int nbr_dtype, int batch, int npad, int32_t* gather_idx_out,
+                          int32_t* status, void* stream);
+/* pair_out (B, S, S) uint8, S = 8 + Npad: bias row of every (query, key). */
+int sb_build_pair_u8(const void* coords, int coords_dtype, const void* mask, int mask_dtype, int batch,
+                     int npad, const uint8_t* lut, uint8_t* pair_out, void* stream);
+
+/* ---- kernel-op boundary (torch.library ops of the reference) ------------- */
+/* shrimp::hex_conv (_triton_conv.py:93-128): out = (gather7(x) @ W + b) * mask.
+ * x (B, Npad, Cin) f16, gather_idx (B, Npad, 7) int32 row-local (Npad = zero
+ * row), mask (B, Npad) u8, w packed by sb_pack_hex_conv_weight, out f16. */
+int sb_hex_conv(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w_packed,
+                const float* bias, int batch, int npad, int cin, int cout, void* out, void* workspace,
+                size_t workspace_bytes, void* stream);
+/* shrimp::hex_conv_ln (_triton_conv.py:198-239): LayerNorm(conv) (+ReLU) * mask. */
+int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w_packed,
+                   const float* bias, const float* ln_w, const float* ln_b, float eps, int relu, int batch,
+                   int npad, int cin, int cout, void* out, void* workspace, size_t workspace_bytes,
+                   void* stream);
+/* Workspace for sb_hex_conv / sb_hex_conv_ln. */
+int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes);
+/* shrimp::attn_pair (_triton_attn.py:132-171): q, k, v (B, H, S, D) f16 with
+ * unit stride on D, pair (B, S, S) uint8, table2 (238, H) f32, out (B, H, S, D). */
+int sb_attn_pair(const void* q, const void* k, const void* v, const uint8_t* pair, const float* table2,
+                 int batch, int heads, int seq, int head_dim, void* out, void* stream);
+
+/* ---- weight packing ------------------------------------------------------ */
+/* HexNodeConv weight (taps, Cin, Cout) fp32 -> f16 [Cout][Kpad], Kpad =
+ * roundup(taps * cin_pad, 64), channel c >= Cin of each tap zero. */
+int sb_pack_hex_conv_weight(const float* w, int taps, int cin, int cin_pad, int cout, void* out, void* stream);
+/* nn.Linear weight (N, K) fp32 -> f16 [N][Kpad]. */
+int sb_pack_linear_weight(const float* w, int n, int k, void* out, void* stream);
+
+/* ---- decode (losses.py:40-61, inference.py:998-1042) ---------------------- */
+int sb_decode_binned(const float* logits, int batch, float scale, float offset, float* out, void* stream);
+/* priors_out[row_offsets[b] + i] = softmax(policy[b, :legal[b]])[i]. */
+int sb_legal_prefix_softmax(const float* policy, int batch, int npad, const int32_t* legal_counts,
+                            const int64_t* row_offsets, float* priors_out, void* stream);
+
+/* ---- microbench kernels (BASELINE configs 2 and 3) ------------------------ */
+/* out = relu(gather_T(x) @ W + b + x); x (B, N, C) bf16, nbr (N, T) int32 (-1 = off support),
+ * W packed [C][Kpad] bf16. Workspace: B * N * T int32. */
+int sb_raytap_conv(const void* x, const int32_t* nbr, int taps, const void* w_packed, const float* bias,
+                   int batch, int n, int c, void* out, void* workspace, size_t workspace_bytes, void* stream);
+/* out = softmax(Q.K^T / sqrt(d) + table[offset_map, h]) V; q, k, v, out (B, L, H*d) bf16. */
+int sb_offset_attention(const void* q, const void* k, const void* v, const float* table, int table_rows,
+                        const int32_t* offset_map, int batch, int len, int heads, int head_dim, void* out,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHRIMP_B200_H_ */

@@ -1,0 +1,293 @@
+"""Parity of the native CUDA path against the CPU oracle and the reference's
+golden outputs. Every call goes through the C ABI (hexo_bot_b200._lib).
+
+Tolerances: policy logits max-abs <= 2e-2 over real
+cells, decoded value max-abs <= 1e-2, legal-prefix policy argmax agreement
+>= 99.5 %; index tables bit-exact.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import GOLDEN
+from hexo_bot_b200 import _lib
+from hexo_bot_b200 import positions as P
+from hexo_bot_b200.geometry import cell_bias_lut
+from hexo_bot_b200.model import ShrimpNet
+from oracle import forward as O
+
+pytestmark = pytest.mark.gpu
+
+POLICY_TOL = 2e-2
+VALUE_TOL = 1e-2
+ARGMAX_MIN = 0.995
+
+SMOKE = dict(channels=32, attention_heads=4, trunk_layout="CCA")
+MAIN = dict(channels=128, attention_heads=8, trunk_layout="CCACCACCACCA")
+STRESS = dict(channels=192, attention_heads=12, trunk_layout="CCACCACCACCA")
+DEFAULT = dict(channels=96, attention_heads=4, trunk_layout="CCCACCCACCA")
+
+DEV = torch.device("cuda:0")
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def build(kw, seed, derandomized):
+    torch.manual_seed(seed)
+    m = ShrimpNet(**kw)
+    sd = m.state_dict()
+    if derandomized:
+        sd = O.derandomize(sd)
+        m.load_state_dict(sd)
+    return m.to(DEV), {k: v.clone() for k, v in sd.items()}
+
+
+def run(model, batch, **kw):
+    ins = [batch[k].to(DEV) for k in ("feats", "nbr", "mask", "coords")]
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = model.forward_policy_value(*ins, request_moves_left=True, status=status, **kw)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    return {k: v.cpu() for k, v in out.items()}
+
+
+def check_against(out, ref, batch):
+    mask = batch["mask"].bool()
+    pol = ((out["policy"] - ref["policy"]).abs() * mask).max().item()
+    assert pol <= POLICY_TOL, f"policy max-abs {pol}"
+    if (~mask).any():
+        assert out["policy"][~mask].abs().max().item() == 0.0, "pad logits must be exactly 0"
+    dv = (O.decode_binned_value(out["value"]) - O.decode_binned_value(ref["value"])).abs().max().item()
+    assert dv <= VALUE_TOL, f"value max-abs {dv}"
+    dml = (out["moves_left"] - ref["moves_left"]).abs().max().item()
+    assert dml <= 5e-2, f"moves-left logits max-abs {dml}"
+    lc = batch["legal_counts"]
+    agree = sum(
+        int(out["policy"][i, : lc[i]].argmax() == ref["policy"][i, : lc[i]].argmax()) for i in range(len(lc))
+    ) / len(lc)
+    assert agree >= ARGMAX_MIN, f"argmax agreement {agree}"
+    return pol, dv, agree
+
+
+@pytest.mark.parametrize("name", ["smoke", "main", "stress"])
+def test_forward_matches_reference_golden(name):
+    rec = torch.load(GOLDEN / f"forward_{name}.pt", weights_only=False)
+    cfg = rec["config"]
+    kw = {k: cfg[k] for k in ("channels", "attention_heads", "trunk_layout")}
+    for mode in ("default", "derandomized"):
+        model, _ = build(kw, cfg["seed"], mode == "derandomized")
+        for (m, bname), case in rec["cases"].items():
+            if m != mode:
+                continue
+            out = run(model, case["inputs"])
+            check_against(out, case, case["inputs"])
+
+
+@pytest.mark.parametrize(
+    "kw,seed,batch_fn",
+    [
+        (SMOKE, 0, lambda: P.disk_batch(64, 0, 30, 4)),
+        (SMOKE, 0, lambda: P.support_batch(16, 5, 30, 4)),
+        (MAIN, 0, lambda: P.disk_batch(32, 0, 60, 4)),
+        (STRESS, 1, lambda: P.disk_batch(6, 1, 120, 8)),
+        (DEFAULT, 2, lambda: P.support_batch(6, 2, 20, 8)),
+    ],
+)
+@pytest.mark.parametrize("derandomized", [False, True])
+def test_forward_matches_oracle(kw, seed, batch_fn, derandomized):
+    batch = batch_fn()
+    model, sd = build(kw, seed, derandomized)
+    out = run(model, batch)
+    ref = O.forward_policy_value(sd, batch["feats"], batch["nbr"], batch["mask"], batch["coords"],
+                                 heads=kw["attention_heads"], layout=kw["trunk_layout"], request_moves_left=True)
+    check_against(out, ref, batch)
+
+
+def test_input_dtype_variants_agree():
+    batch = P.support_batch(8, 3, 20, 4)
+    model, _ = build(SMOKE, 0, True)
+    base = run(model, batch)
+    alt = dict(batch)
+    alt["feats"] = batch["feats"].half()
+    alt["nbr"] = batch["nbr"].int()
+    alt["coords"] = batch["coords"].int()
+    out = run(model, alt)
+    assert torch.equal(out["policy"], base["policy"]) and torch.equal(out["value"], base["value"])
+
+
+def test_full_size_properties_main():
+    """Batch 4096 (the bench size): finite, pad-free disk rows, and each
+    position's outputs independent of the rest of the batch (bit-exact)."""
+    base = P.disk_batch(512, 0, 60, 4)
+    batch = P.tile_batch(base, 8)
+    model, _ = build(MAIN, 0, True)
+    full = run(model, batch)
+    assert torch.isfinite(full["policy"]).all() and torch.isfinite(full["value"]).all()
+    part = run(model, {k: v[1024:1536] for k, v in batch.items()})
+    assert torch.equal(full["policy"][1024:1536], part["policy"])
+    assert torch.equal(full["value"][1024:1536], part["value"])
+    # tiled copies of the same positions give identical outputs
+    assert torch.equal(full["policy"][:512], full["policy"][3584:])
+    again = run(model, batch)
+    assert torch.equal(again["policy"], full["policy"]) and torch.equal(again["value"], full["value"])
+
+
+def test_weights_repack_after_update():
+    batch = P.disk_batch(4, 0, 30, 4)
+    model, _ = build(SMOKE, 0, False)
+    a = run(model, batch)
+    with torch.no_grad():
+        model.value_head.bias.add_(1.0)
+    b = run(model, batch)
+    assert (b["value"] - a["value"] - 1.0).abs().max().item() < 1e-4
+
+
+def test_out_of_range_neighbour_sets_status_without_fault():
+    batch = P.disk_batch(2, 0, 10, 4)
+    batch["nbr"] = batch["nbr"].clone()
+    batch["nbr"][0, 0, 0] = 10_000
+    model, _ = build(SMOKE, 0, False)
+    ins = [batch[k].to(DEV) for k in ("feats", "nbr", "mask", "coords")]
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = model.forward_policy_value(*ins, status=status)
+    torch.cuda.synchronize()
+    assert status.item() & 2
+    assert torch.isfinite(out["policy"]).all()
+
+
+def test_index_tables_bit_exact():
+    t = torch.load(GOLDEN / "tables.pt", weights_only=False)
+    for batch in (t["batch"], P.support_batch(6, 11, 30, 4), P.disk_batch(8, 3, 60, 4)):
+        coords = batch["coords"].to(DEV)
+        mask = batch["mask"].to(DEV)
+        nbr = batch["nbr"].to(DEV)
+        b, n = mask.shape
+        lut = torch.from_numpy(cell_bias_lut().copy()).to(DEV)
+        pair = torch.empty(b, n + 8, n + 8, dtype=torch.uint8, device=DEV)
+        _lib.check(_lib.lib().sb_build_pair_u8(coords.data_ptr(), _lib.DT_I64, mask.data_ptr(), _lib.DT_U8, b, n,
+                                               lut.data_ptr(), pair.data_ptr(), stream()), "pair")
+        g = torch.empty(b, n, 7, dtype=torch.int32, device=DEV)
+        _lib.check(_lib.lib().sb_build_gather_index(nbr.data_ptr(), _lib.DT_I64, b, n, g.data_ptr(), None,
+                                                    stream()), "gidx")
+        torch.cuda.synchronize()
+        assert torch.equal(pair.cpu(), O.build_pair_u8(batch["coords"], batch["mask"]))
+        assert torch.equal(g.cpu().long(), O.gather_index(batch["nbr"]))
+
+
+def _pack_conv(w, cin_pad=None):
+    taps, cin, cout = w.shape
+    cin_pad = cin_pad or cin
+    kpad = (taps * cin_pad + 63) // 64 * 64
+    out = torch.empty(cout, kpad, dtype=torch.float16, device=DEV)
+    _lib.check(_lib.lib().sb_pack_hex_conv_weight(w.data_ptr(), taps, cin, cin_pad, cout, out.data_ptr(),
+                                                  stream()), "pack")
+    return out
+
+
+@pytest.mark.parametrize("b,n,cin,cout", [(3, 61, 32, 32), (5, 61, 128, 128), (2, 100, 192, 192), (4, 33, 16, 64)])
+def test_hex_conv_ops_match_fp32(b, n, cin, cout):
+    torch.manual_seed(0)
+    x = torch.randn(b, n, cin, device=DEV).half()
+    nbr = torch.randint(0, n + 1, (b, n, 6), device=DEV)
+    gidx = torch.cat([torch.arange(n, device=DEV).view(1, n, 1).expand(b, -1, -1), nbr], 2).int().contiguous()
+    mask = (torch.rand(b, n, device=DEV) > 0.1).to(torch.uint8)
+    w = torch.randn(7, cin, cout, device=DEV) / math.sqrt(7 * cin)
+    bias = torch.randn(cout, device=DEV) * 0.1
+    wp = _pack_conv(w)
+    out = torch.empty(b, n, cout, dtype=torch.float16, device=DEV)
+    nb = C.c_size_t()
+    _lib.lib().sb_hex_conv_workspace_bytes(b, n, C.byref(nb))
+    ws = torch.empty(nb.value, dtype=torch.uint8, device=DEV)
+    lib = _lib.lib()
+    _lib.check(lib.sb_hex_conv(x.data_ptr(), gidx.data_ptr(), mask.data_ptr(), wp.data_ptr(), bias.data_ptr(), b, n,
+                               cin, cout, out.data_ptr(), ws.data_ptr(), nb.value, stream()), "hex_conv")
+    conv = O.hex_conv(x.float().cpu(), gidx.long().cpu(), mask.bool().cpu(), w.half().float().cpu(), bias.cpu())
+    torch.cuda.synchronize()
+    assert (out.float().cpu() - conv).abs().max().item() <= 1e-2
+    lw = torch.rand(cout, device=DEV) + 0.5
+    lb = torch.randn(cout, device=DEV) * 0.1
+    _lib.check(lib.sb_hex_conv_ln(x.data_ptr(), gidx.data_ptr(), mask.data_ptr(), wp.data_ptr(), bias.data_ptr(),
+                                  lw.data_ptr(), lb.data_ptr(), 1e-5, 1, b, n, cin, cout, out.data_ptr(),
+                                  ws.data_ptr(), nb.value, stream()), "hex_conv_ln")
+    ref = F.relu(F.layer_norm(conv, (cout,), lw.cpu(), lb.cpu(), 1e-5)) * mask.bool().cpu().unsqueeze(-1)
+    torch.cuda.synchronize()
+    assert (out.float().cpu() - ref).abs().max().item() <= 1e-2
+
+
+@pytest.mark.parametrize("b,h,s,d", [(3, 4, 69, 8), (2, 8, 69, 16), (2, 4, 130, 32), (2, 2, 40, 24), (1, 3, 225, 64)])
+def test_attn_pair_matches_fp32(b, h, s, d):
+    torch.manual_seed(1)
+    q = torch.randn(b, h, s, d, device=DEV).half()
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    pair = torch.randint(0, 238, (b, s, s), device=DEV, dtype=torch.uint8)
+    pair[:, :, :3] = torch.randint(0, 237, (b, s, 3), device=DEV, dtype=torch.uint8)
+    table = torch.randn(238, h, device=DEV) * 0.5
+    table[237] = -3e4
+    out = torch.empty_like(q)
+    _lib.check(_lib.lib().sb_attn_pair(q.data_ptr(), k.data_ptr(), v.data_ptr(), pair.data_ptr(), table.data_ptr(),
+                                       b, h, s, d, out.data_ptr(), stream()), "attn_pair")
+    bias = table[pair.long()].permute(0, 3, 1, 2)
+    ref = torch.softmax(q.float() @ k.float().transpose(-1, -2) / math.sqrt(d) + bias, -1) @ v.float()
+    assert (out.float() - ref).abs().max().item() <= 5e-3
+
+
+def test_raytap_conv_microbench_matches_oracle():
+    torch.manual_seed(3)
+    b, n, c, t = 8, 61, 128, 19
+    x = torch.randn(b, n, c, device=DEV).bfloat16()
+    nbr = torch.randint(-1, n, (n, t), device=DEV, dtype=torch.int32)
+    nbr[:, 0] = torch.arange(n, device=DEV)
+    w = torch.randn(t * c, c, device=DEV) / math.sqrt(t * c)
+    bias = torch.randn(c, device=DEV) * 0.1
+    wp = w.t().contiguous().bfloat16()
+    ws = torch.empty(b * n * t * 4, dtype=torch.uint8, device=DEV)
+    out = torch.empty_like(x)
+    _lib.check(_lib.lib().sb_raytap_conv(x.data_ptr(), nbr.data_ptr(), t, wp.data_ptr(), bias.data_ptr(), b, n, c,
+                                         out.data_ptr(), ws.data_ptr(), ws.numel(), stream()), "raytap")
+    ref = O.raytap_conv(x.float().cpu(), nbr.cpu(), w.bfloat16().float().cpu(), bias.cpu())
+    torch.cuda.synchronize()
+    # bf16 output rounding of values up to ~6 dominates
+    assert ((out.float().cpu() - ref).abs() / (1 + ref.abs())).max().item() <= 8e-3
+
+
+def test_offset_attention_microbench_matches_oracle():
+    torch.manual_seed(4)
+    b, l, h, d = 16, 61, 8, 32
+    q = torch.randn(b, l, h * d, device=DEV).bfloat16()
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    table = torch.randn(217, h, device=DEV) * 0.5
+    om = torch.randint(0, 217, (l, l), device=DEV, dtype=torch.int32)
+    out = torch.empty_like(q)
+    _lib.check(_lib.lib().sb_offset_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), table.data_ptr(), 217,
+                                              om.data_ptr(), b, l, h, d, out.data_ptr(), stream()), "offattn")
+    ref = O.offset_bias_attention(q.float().cpu(), k.float().cpu(), v.float().cpu(), table.cpu(), om.cpu(), h)
+    torch.cuda.synchronize()
+    assert (out.float().cpu() - ref).abs().max().item() <= 2e-2
+
+
+def test_decode_kernels_match_oracle():
+    torch.manual_seed(5)
+    logits = (torch.randn(37, 65) * 2).to(DEV)
+    out = torch.empty(37, device=DEV)
+    _lib.check(_lib.lib().sb_decode_binned(logits.data_ptr(), 37, 1.0, 0.0, out.data_ptr(), stream()), "decode")
+    torch.cuda.synchronize()
+    assert (out.cpu() - O.decode_binned_value(logits.cpu())).abs().max().item() <= 1e-6
+    policy = torch.randn(5, 40).to(DEV)
+    legal = torch.tensor([1, 40, 7, 0, 13], dtype=torch.int32)
+    offs = torch.cumsum(torch.cat([torch.zeros(1, dtype=torch.int64), legal.long()]), 0)[:-1]
+    pri = torch.empty(int(legal.sum()), device=DEV)
+    _lib.check(_lib.lib().sb_legal_prefix_softmax(policy.data_ptr(), 5, 40, legal.to(DEV).data_ptr(),
+                                                  offs.to(DEV).data_ptr(), pri.data_ptr(), stream()), "softmax")
+    torch.cuda.synchronize()
+    ref = torch.cat(O.legal_prefix_priors(policy.cpu(), legal))
+    assert (pri.cpu() - ref).abs().max().item() <= 1e-6
