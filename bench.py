@@ -255,6 +255,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="override the global batch")
     ap.add_argument("--no-latency", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["conv"], default=None,
+                    help="time only the dominant kernel at the bench shape (for profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = dict(CONFIGS[args.config])
@@ -283,6 +285,12 @@ def main():
     model = build_model(cfg, device, rank, world)
     npad = host["feats"].shape[1]
     dev_in = [host[k].to(device) for k in ("feats", "nbr", "mask", "coords")]
+    if args.kernel == "conv":
+        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+        r = conv_roofline(model, dev_in, cfg, shard, npad, device, flush, steps=args.steps, warmup=args.warmup)
+        if rank == 0:
+            print(json.dumps({"kernel_only": r}), flush=True)
+        return
     out = {
         "policy": torch.empty(shard, npad, dtype=torch.float32, device=device),
         "value": torch.empty(shard, 65, dtype=torch.float32, device=device),
@@ -407,7 +415,7 @@ def main():
         dist.destroy_process_group()
 
 
-def conv_roofline(model, dev_in, cfg, shard, npad, device, flush) -> dict:
+def conv_roofline(model, dev_in, cfg, shard, npad, device, flush, steps=20, warmup=3) -> dict:
     """Time the trunk's gather-GEMM conv (conv + LN + ReLU epilogue, the kernel
     that carries ~70 % of the FLOPs) alone at the bench shape via the C ABI."""
 
@@ -441,7 +449,7 @@ def conv_roofline(model, dev_in, cfg, shard, npad, device, flush) -> dict:
                                       lw.data_ptr(), lb.data_ptr(), 1e-5, 1, shard, npad, c, c, out.data_ptr(),
                                       ws.data_ptr(), nb.value, torch.cuda.current_stream().cuda_stream), "conv")
 
-    times = time_steps(call, 20, 3, flush)
+    times = time_steps(call, steps, warmup, flush)
     ms = statistics.mean(times)
     flops = 2.0 * shard * npad * 7 * c * c
     peaks = load_peaks()
