@@ -1,10 +1,12 @@
 // C ABI of shrimp_b200 (declared in include/shrimp_b200.h): argument checks,
 // workspace layout, kernel launches and the ShrimpNet serve-forward schedule.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -28,8 +30,25 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+// SHRIMP_B200_SYNC_DEBUG=1: synchronise and log after every launch (debugging
+// aid; never set in serving).
+bool sync_debug() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("SHRIMP_B200_SYNC_DEBUG");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 int check_launch(const char* what) {
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && sync_debug()) {
+    fprintf(stderr, "[sb] launched %s ...", what);
+    fflush(stderr);
+    e = cudaDeviceSynchronize();
+    fprintf(stderr, " done (%s)\n", cudaGetErrorString(e));
+  }
   if (e != cudaSuccess) return fail(SB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return SB_OK;
 }
@@ -40,11 +59,11 @@ inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
 // N tile for an n-wide GEMM: one tile when n <= 256, else the fewest equal
 // tiles (multiples of 16) of at most 256 columns.
 int choose_bn(int n) {
-  if (n % 16 != 0) return -1;
-  for (int k = 1; k <= 16; ++k) {
+  if (n % 32 != 0) return -1;
+  for (int k = 1; k <= 32; ++k) {
     if (n % k) continue;
     const int bn = n / k;
-    if (bn <= 256 && bn % 16 == 0) return bn;
+    if (bn <= 256 && bn % 32 == 0) return bn;
   }
   return -1;
 }
@@ -64,29 +83,100 @@ int ensure_smem(const void* fn, int bytes) {
   return SB_OK;
 }
 
-template <typename T, int STAGES>
-int launch_gemm_stages(const GemmArgs& a, cudaStream_t st) {
-  const int smem = gemm_smem_bytes(a.bn, STAGES);
-  if (int s = ensure_smem(reinterpret_cast<const void*>(gemm_tc_kernel<T, STAGES>), smem)) return s;
-  dim3 grid((unsigned)cdiv(a.M, kBlockM), (unsigned)(a.n_total / a.bn));
-  gemm_tc_kernel<T, STAGES><<<grid, kGemmThreads, smem, st>>>(a);
-  return check_launch("gemm_tc_kernel");
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2D row-major 16-bit tensor map, 128-byte swizzle, box {64 columns, box_rows}.
+int make_tmap(CUtensorMap* m, const void* ptr, bool bf16, long long cols, long long rows, long long row_elems,
+              int box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_elems * 2};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SB_OK;
+}
+
+// Operand producer of the tensor-core GEMM: 0 = TMA (gather4 rows + 2D weight
+// tiles) whenever the shapes allow it, 1 = cp.async everywhere. Read once from
+// SHRIMP_B200_GEMM_PRODUCER ("tma" | "cpasync").
+int producer_mode() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("SHRIMP_B200_GEMM_PRODUCER");
+    mode = (e && strcmp(e, "cpasync") == 0) ? 1 : 0;
+  }
+  return mode;
+}
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
 }
 
 template <typename T>
 int launch_gemm(GemmArgs a, cudaStream_t st) {
   if (a.M <= 0) return SB_OK;
   if (a.bn <= 0) a.bn = choose_bn(a.n_total);
-  if (a.bn <= 0 || a.bn > 256 || a.bn % 16 || a.n_total % a.bn)
-    return fail(SB_ERR_UNSUPPORTED, "gemm: N=%d cannot be tiled (need a multiple of 16)", a.n_total);
+  if (a.bn <= 0 || a.bn > 256 || a.bn % 32 || a.n_total % a.bn)
+    return fail(SB_ERR_UNSUPPORTED, "gemm: N=%d cannot be tiled (need a multiple of 32)", a.n_total);
   if (a.kpad % kChunkK || a.kpad < a.taps * a.cin)
     return fail(SB_ERR_INVALID_ARG, "gemm: kpad=%d must be a multiple of 64 covering taps*cin=%d", a.kpad,
                 a.taps * a.cin);
   if (a.cin % 8) return fail(SB_ERR_UNSUPPORTED, "gemm: input channels per tap (%d) must be a multiple of 8", a.cin);
-  if ((a.flags & (EPI_LN_A | EPI_LN_B | EPI_HEAD)) && a.bn != a.n_total)
+  if (a.taps < 1 || a.taps > kMaxTaps) return fail(SB_ERR_UNSUPPORTED, "gemm: %d taps > %d", a.taps, kMaxTaps);
+  if (!a.gidx && a.taps != 1) return fail(SB_ERR_INVALID_ARG, "gemm: identity rows need taps == 1");
+  if ((a.flags & (EPI_LN_A | EPI_LN_B | EPI_HEAD | EPI_RESID)) && a.bn != a.n_total)
     return fail(SB_ERR_UNSUPPORTED, "gemm: row-wise epilogue needs N=%d <= 256", a.n_total);
-  if (a.bn <= 128) return launch_gemm_stages<T, 6>(a, st);
-  return launch_gemm_stages<T, 4>(a, st);
+  if (a.n_total > 1024) return fail(SB_ERR_UNSUPPORTED, "gemm: N=%d > 1024", a.n_total);
+  if (a.a_rows <= 0) a.a_rows = a.gidx ? (1LL << 31) - 1 : a.M;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap ma, mb;
+  memset(&ma, 0, sizeof(ma));
+  memset(&mb, 0, sizeof(mb));
+  a.use_tma = (a.cin % kChunkK == 0) && (a.lda % 8 == 0) && ((uintptr_t)a.A % 16 == 0) &&
+              ((uintptr_t)a.Bw % 16 == 0) && a.a_rows < (1LL << 31) - 1 && producer_mode() != 1;
+  if (a.use_tma) {
+    if (int s = make_tmap(&ma, a.A, bf16, a.lda, a.a_rows, a.lda, a.gidx ? 1 : kBlockM)) return s;
+    if (int s = make_tmap(&mb, a.Bw, bf16, a.kpad, a.n_total, a.kpad, a.bn)) return s;
+  }
+  const int stages = gemm_stages(a.bn, a.taps);
+  const int smem = gemm_smem_bytes(a.bn, stages, a.taps);
+  if (int s = ensure_smem(reinterpret_cast<const void*>(gemm_ws_kernel<T>), smem)) return s;
+  const long long tiles = cdiv(a.M, kBlockM) * (a.n_total / a.bn);
+  const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  gemm_ws_kernel<T><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, stages);
+  if (sync_debug())
+    fprintf(stderr, "[sb] gemm M=%d N=%d bn=%d kpad=%d taps=%d cin=%d tma=%d stages=%d smem=%d grid=%d flags=%d\n",
+            a.M, a.n_total, a.bn, a.kpad, a.taps, a.cin, a.use_tma, stages, smem, grid, a.flags);
+  return check_launch("gemm_ws_kernel");
 }
 
 template <typename T>
@@ -116,6 +206,10 @@ int launch_attention(const AttnArgs& a, cudaStream_t st) {
 
 // ---- forward workspace --------------------------------------------------------
 
+// Readable bytes kept after every gather table (the GEMM prefetches it in
+// whole 16-byte pieces).
+constexpr size_t kGidxSlack = 64;
+
 struct FwdLayout {
   size_t seq32, lnf32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, total;
 };
@@ -139,7 +233,7 @@ FwdLayout fwd_layout(int C, int B, int npad) {
   L.o16 = take(R * C * 2);
   L.u16 = take(R * 2 * C * 2);
   L.feat16 = take(R * kFeatPad * 2);
-  L.gidx = take(Mc * 7 * 4);
+  L.gidx = take(Mc * 7 * 4 + kGidxSlack);
   L.rowmask = take(R * 4);
   L.coords32 = take(Mc * 2 * 4);
   L.total = off;
@@ -247,14 +341,14 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
 
   auto conv_args = [&](const void* x, const void* w, const float* bias) {
     GemmArgs g{};
-    g.A = x; g.lda = C; g.cin = C; g.taps = 7; g.gidx = gidx; g.M = (int)Mc;
+    g.A = x; g.lda = C; g.a_rows = R; g.cin = C; g.taps = 7; g.gidx = gidx; g.M = (int)Mc; g.orow_from_gidx = 1;
     g.Bw = w; g.kpad = round_up(7 * C, kChunkK); g.n_total = C; g.bn = C;
     g.bias = bias; g.eps = eps; g.rowmask = rowmask; g.seq_len = S; g.ntok = kNumTok; g.err = err;
     return g;
   };
   auto linear_args = [&](const void* x, int k, const void* w, int n, const float* bias) {
     GemmArgs g{};
-    g.A = x; g.lda = k; g.cin = k; g.taps = 1; g.gidx = nullptr; g.M = (int)R;
+    g.A = x; g.lda = k; g.a_rows = R; g.cin = k; g.taps = 1; g.gidx = nullptr; g.M = (int)R;
     g.Bw = w; g.kpad = round_up(k, kChunkK); g.n_total = n; g.bn = 0;
     g.bias = bias; g.eps = eps; g.rowmask = rowmask; g.seq_len = S; g.ntok = kNumTok; g.err = err;
     return g;
@@ -385,7 +479,7 @@ int sb_build_pair_u8(const void* coords, int coords_dtype, const void* mask, int
 int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes) {
   if (!bytes || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "hex_conv workspace: bad args");
   const size_t rows = (size_t)batch * npad;
-  *bytes = ((rows * 7 * 4 + 255) & ~size_t(255)) + rows * 4;
+  *bytes = ((rows * 7 * 4 + kGidxSlack + 255) & ~size_t(255)) + rows * 4;
   return SB_OK;
 }
 
@@ -402,13 +496,14 @@ static int hex_conv_common(const void* x, const int32_t* gather_idx, const uint8
   if (rows == 0) return SB_OK;
   cudaStream_t st = (cudaStream_t)stream;
   int32_t* gabs = reinterpret_cast<int32_t*>(workspace);
-  float* rm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + ((rows * 7 * 4 + 255) & ~255LL));
+  float* rm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
+                                      ((rows * 7 * 4 + (long long)kGidxSlack + 255) & ~255LL));
   absolute_gidx_kernel<<<(unsigned)cdiv(rows * 7, 256), 256, 0, st>>>(gather_idx, batch, npad, 7, gabs);
   if (int s = check_launch("absolute_gidx_kernel")) return s;
   mask_to_float_kernel<<<(unsigned)cdiv(rows, 256), 256, 0, st>>>(mask, rows, rm);
   if (int s = check_launch("mask_to_float_kernel")) return s;
   GemmArgs g{};
-  g.A = x; g.lda = cin; g.cin = cin; g.taps = 7; g.gidx = gabs; g.M = (int)rows;
+  g.A = x; g.lda = cin; g.a_rows = rows; g.cin = cin; g.taps = 7; g.gidx = gabs; g.M = (int)rows;
   g.Bw = w; g.kpad = round_up(7 * cin, kChunkK); g.n_total = cout; g.bn = 0;
   g.bias = bias; g.ln_a_w = ln_w; g.ln_a_b = ln_b; g.eps = eps; g.rowmask = rm;
   g.flags = flags | EPI_MASK | EPI_OUT16; g.out16 = out; g.ld16 = cout;
@@ -482,7 +577,7 @@ int sb_legal_prefix_softmax(const float* policy, int batch, int npad, const int3
 int sb_raytap_conv(const void* x, const int32_t* nbr, int taps, const void* w, const float* bias, int batch, int n,
                    int c, void* out, void* workspace, size_t workspace_bytes, void* stream) {
   if (!x || !nbr || !w || !bias || !out || batch < 0 || n <= 0 || taps <= 0) return fail(SB_ERR_INVALID_ARG, "raytap: bad args");
-  const size_t need = (size_t)batch * n * taps * 4;
+  const size_t need = (size_t)batch * n * taps * 4 + kGidxSlack;
   if (!workspace || workspace_bytes < need) return fail(SB_ERR_WORKSPACE, "raytap: workspace < %zu", need);
   if (batch == 0) return SB_OK;
   cudaStream_t st = (cudaStream_t)stream;
@@ -490,7 +585,7 @@ int sb_raytap_conv(const void* x, const int32_t* nbr, int taps, const void* w, c
   shared_gidx_kernel<<<(unsigned)cdiv((long long)batch * n * taps, 256), 256, 0, st>>>(nbr, batch, n, taps, g);
   if (int s = check_launch("shared_gidx_kernel")) return s;
   GemmArgs a{};
-  a.A = x; a.lda = c; a.cin = c; a.taps = taps; a.gidx = g; a.M = batch * n;
+  a.A = x; a.lda = c; a.a_rows = (long long)batch * n; a.cin = c; a.taps = taps; a.gidx = g; a.M = batch * n;
   a.Bw = w; a.kpad = round_up(taps * c, kChunkK); a.n_total = c; a.bn = 0;
   a.bias = bias; a.flags = EPI_RES16 | EPI_OUT16; a.res16 = x; a.ldr16 = c; a.out16 = out; a.ld16 = c;
   return launch_gemm<__nv_bfloat16>(a, st);

@@ -12,7 +12,7 @@
 
 namespace sb {
 
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kSpinLimit = 1u << 30;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -51,10 +51,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Wall-clock bound of every mbarrier wait: far above any legitimate wait
+// (microseconds), short enough that a broken pipeline unwinds quickly.
+constexpr uint64_t kWaitLimitNs = 200ull * 1000 * 1000;
+
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && global_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return false;
+}
+
+// Bounded wait with a short sleep between polls, for waiters off the
+// tensor-core issue path (producers, epilogue): keeps spinning warps from
+// taking issue slots from the warps sharing their scheduler.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(32);
+    if ((i & 63) == 63 && global_ns() - t0 > kWaitLimitNs) return false;
   }
   return false;
 }
@@ -87,6 +113,42 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Accumulating form (D += A * B^T) without a predicate.
+__device__ __forceinline__ void tc_mma_f16_acc(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;\n" ::"r"(d_tmem), "l"(adesc), "l"(bdesc),
+               "r"(idesc)
+               : "memory");
+}
+// A operand from TMEM (128 lanes = rows, 32-bit columns holding two 16-bit K
+// elements, even K in the low half), B from shared memory.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16_ts_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;\n" ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc),
+               "r"(idesc)
+               : "memory");
+}
+// 32 lanes x 32 columns store (thread i -> lane base + i), then wait.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
 // Arrive (once) on an mbarrier when all previously issued tcgen05 ops of this
 // thread have completed.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
@@ -95,9 +157,12 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
 }
 
 // 32 lanes x 32-bit, 16 consecutive columns: thread i of the warp receives
-// lane (base lane + i), columns [col, col+16).
+// lane (base lane + i), columns [col, col+16). Both instructions are
+// .sync.aligned: the whole warp must execute them converged, which the
+// leading __syncwarp() re-establishes after any divergent code before it.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
@@ -131,6 +196,64 @@ __host__ __device__ constexpr uint32_t mma_idesc(int n, bool is_bf16) {
          | ((is_bf16 ? 1u : 0u) << 10)               // B format
          | ((uint32_t)(n >> 3) << 17)                // N >> 3
          | ((uint32_t)(128 >> 4) << 24);             // M >> 4
+}
+
+
+// ---- predicated global accesses ------------------------------------------------
+// Lane-dependent stores / loads as single predicated instructions, so code
+// around tcgen05 .sync.aligned instructions never branches on the lane.
+__device__ __forceinline__ void st_global_v4_if(void* p, uint4 v, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+      "@q st.global.v4.b32 [%0], {%1, %2, %3, %4};\n\t}\n" ::"l"(p),
+      "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"((int)pred)
+      : "memory");
+}
+__device__ __forceinline__ void st_global_f32_if(float* p, float v, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+      "@q st.global.f32 [%0], %1;\n\t}\n" ::"l"(p),
+      "f"(v), "r"((int)pred)
+      : "memory");
+}
+// Returns zeros where pred is false.
+__device__ __forceinline__ uint4 ld_global_v4_if(const void* p, bool pred) {
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+      "@q ld.global.v4.b32 {%0, %1, %2, %3}, [%4];\n\t}\n"
+      : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
+      : "l"(p), "r"((int)pred)
+      : "memory");
+  return v;
+}
+
+// ---- TMA (bulk tensor copies, completion on an mbarrier) --------------------
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+// 2D tiled load of box {c0.., c1..} into shared memory.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
+      ::"r"(dst), "l"(tmap), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+// Four rows (r0..r3, each one box of the map's inner width) gathered into four
+// consecutive 128-byte shared-memory rows; out-of-range rows read as zero.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, int col, int r0, int r1, int r2, int r3,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n"
+      ::"r"(dst), "l"(tmap), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(tmap) : "memory");
 }
 
 // ---- warp-level mma.sync (used by the attention core) -----------------------

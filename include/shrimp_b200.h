@@ -180,7 +180,7 @@ int sb_legal_prefix_softmax(const float* policy, int batch, int npad, const int3
 
 /* ---- microbench kernels (BASELINE configs 2 and 3) ------------------------ */
 /* out = relu(gather_T(x) @ W + b + x); x (B, N, C) bf16, nbr (N, T) int32 (-1 = off support),
- * W packed [C][Kpad] bf16. Workspace: B * N * T int32. */
+ * W packed [C][Kpad] bf16. Workspace: B * N * T int32 plus 64 bytes. */
 int sb_raytap_conv(const void* x, const int32_t* nbr, int taps, const void* w_packed, const float* bias,
                    int batch, int n, int c, void* out, void* workspace, size_t workspace_bytes, void* stream);
 /* out = softmax(Q.K^T / sqrt(d) + table[offset_map, h]) V; q, k, v, out (B, L, H*d) bf16. */
