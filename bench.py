@@ -45,7 +45,7 @@ METRIC = "Shrimp positions/sec at batch 4096 (1/2/4/8 B200); p50 latency at batc
 LATENCY_BATCHES = (1, 16, 64, 256, 1024)
 # dram bytes (read + write) of one dominant-kernel launch at the bench shape,
 # from the committed ncu capture (profiles/conv_gemm_main.md); None until captured.
-DOMINANT_TRAFFIC_BYTES = None
+DOMINANT_TRAFFIC_BYTES = 99_334_144
 
 
 def load_peaks() -> dict:
@@ -122,30 +122,15 @@ def make_batch(cfg: dict, count: int, start: int):
     return positions.disk_batch(count, cfg["seed"], cfg["plies"], cfg["disk"], start=start)
 
 
-def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
-    """Contiguous position shard of rank `rank` (sizes differ by at most one)."""
-
-    base, extra = divmod(total, world)
-    lo = rank * base + min(rank, extra)
-    return lo, lo + base + (1 if rank < extra else 0)
-
-
 def build_model(cfg: dict, device, rank: int, world: int):
     from hexo_bot_b200.model import ShrimpNet
+    from hexo_bot_b200.sharding import broadcast_weights
 
     kw = {k: cfg[k] for k in ("channels", "attention_heads", "trunk_layout")}
     torch.manual_seed(cfg["seed"])
     model = ShrimpNet(**kw).to(device)
     if world > 1:
-        # one NCCL broadcast of every parameter from rank 0 (flattened)
-        params = [p.data for p in model.parameters()]
-        flat = torch.cat([p.reshape(-1) for p in params])
-        dist.broadcast(flat, src=0)
-        off = 0
-        for p in params:
-            n = p.numel()
-            p.copy_(flat[off:off + n].view_as(p))
-            off += n
+        broadcast_weights(model, src=0)  # the one NCCL collective of the run
     model.packed(device)
     return model
 
@@ -279,6 +264,8 @@ def main():
     from hexo_bot_b200.model import ShrimpNet
 
     total = cfg["batch"]
+    from hexo_bot_b200.sharding import shard_range
+
     lo, hi = shard_range(total, rank, world)
     shard = hi - lo
     host = make_batch(cfg, shard, lo)
@@ -455,7 +442,7 @@ def conv_roofline(model, dev_in, cfg, shard, npad, device, flush, steps=20, warm
     peaks = load_peaks()
     achieved = flops / (ms / 1e3) / 1e12
     return {
-        "kernel": "gemm_tc_kernel (7-tap gather-GEMM conv + LayerNorm/ReLU epilogue), timed via sb_hex_conv_ln",
+        "kernel": "gemm_ws_kernel (7-tap gather-GEMM conv + LayerNorm/ReLU epilogue), timed via sb_hex_conv_ln",
         "bound": "tensor",
         "achieved": round(achieved, 2),
         "peak": peaks["tflops"],

@@ -110,7 +110,7 @@ def lib() -> C.CDLL:
         "sb_hex_conv": ([_P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P, sz, _P], i32),
         "sb_hex_conv_ln": ([_P, _P, _P, _P, _P, _P, _P, f32, i32, i32, i32, i32, i32, _P, _P, sz, _P], i32),
         "sb_hex_conv_workspace_bytes": ([i32, i32, C.POINTER(sz)], i32),
-        "sb_attn_pair": ([_P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P], i32),
+        "sb_attn_pair": ([_P, _P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P], i32),
         "sb_pack_hex_conv_weight": ([_P, i32, i32, i32, i32, _P, _P], i32),
         "sb_pack_linear_weight": ([_P, i32, i32, _P, _P], i32),
         "sb_decode_binned": ([_P, i32, f32, f32, _P, _P], i32),

@@ -180,18 +180,57 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
 }
 
 template <typename T>
-int launch_attention(const AttnArgs& a, cudaStream_t st) {
+int launch_attention(AttnArgs a, cudaStream_t st) {
   if (a.D % 8 || a.D <= 0 || a.D > 64)
     return fail(SB_ERR_UNSUPPORTED, "attention: head_dim=%d must be a multiple of 8 in [8, 64]", a.D);
-  if (a.table_rows > kMaxTableRows) return fail(SB_ERR_UNSUPPORTED, "attention: %d bias rows > %d", a.table_rows, kMaxTableRows);
-  dim3 grid((unsigned)cdiv(a.S, kAttnBlockQ), (unsigned)a.H, (unsigned)a.B);
+  if (a.table_rows <= 0 || a.table_rows > kMaxTableRows)
+    return fail(SB_ERR_UNSUPPORTED, "attention: %d bias rows (1..%d supported)", a.table_rows, kMaxTableRows);
   const int dp = round_up(a.D, 16);
-#define SB_ATTN_CASE(DPV)                                                                 \
-  case DPV: {                                                                             \
-    const int smem = AttnSmem<DPV>::kBytes;                                               \
-    if (int s = ensure_smem(reinterpret_cast<const void*>(attn_kernel<T, DPV>), smem)) return s; \
-    attn_kernel<T, DPV><<<grid, kAttnThreads, smem, st>>>(a);                            \
-    return check_launch("attn_kernel");                                                   \
+  // Position-resident kernel when the per-position row table and the K/V of at
+  // least one head fit in shared memory: the largest head group that allows
+  // two CTAs per SM, else one CTA per SM. Longer sequences stream.
+  int group = 0;
+  if (a.table_rows <= 255 || a.mode == BIAS_OFFSET) {
+    for (int budget : {113 * 1024, 227 * 1024}) {
+      for (int gsz = a.H; gsz >= 1 && !group; --gsz)
+        if (attn_smem_bytes(a.S, dp, gsz, a.table_rows) <= budget) group = gsz;
+      if (group) break;
+    }
+  }
+  if (group) {
+    a.group = group;
+    const int smem = attn_smem_bytes(a.S, dp, group, a.table_rows);
+    const int per_sm = smem <= 113 * 1024 ? 2 : 1;
+    const int grid = a.B < per_sm * num_sms() ? a.B : per_sm * num_sms();
+    const bool one_pass = attn_pad16(a.S) <= 80;  // all keys in one softmax step
+#define SB_ATTN_CASE(DPV)                                                                       \
+  case DPV: {                                                                                   \
+    const void* fn = one_pass ? reinterpret_cast<const void*>(attn_kernel<T, DPV, 10>)          \
+                              : reinterpret_cast<const void*>(attn_kernel<T, DPV, 4>);          \
+    if (int s = ensure_smem(fn, smem)) return s;                                                \
+    if (one_pass)                                                                               \
+      attn_kernel<T, DPV, 10><<<(unsigned)grid, kAttnThreads, smem, st>>>(a);                   \
+    else                                                                                        \
+      attn_kernel<T, DPV, 4><<<(unsigned)grid, kAttnThreads, smem, st>>>(a);                    \
+    return check_launch("attn_kernel");                                                         \
+  }
+    switch (dp) {
+      SB_ATTN_CASE(16)
+      SB_ATTN_CASE(32)
+      SB_ATTN_CASE(48)
+      SB_ATTN_CASE(64)
+      default: break;
+    }
+#undef SB_ATTN_CASE
+    return fail(SB_ERR_UNSUPPORTED, "attention: head_dim=%d", a.D);
+  }
+  dim3 grid((unsigned)cdiv(a.S, kStreamBlockQ), (unsigned)a.H, (unsigned)a.B);
+#define SB_ATTN_CASE(DPV)                                                                   \
+  case DPV: {                                                                               \
+    const int smem = AttnStreamSmem<DPV>::kBytes;                                           \
+    if (int s = ensure_smem(reinterpret_cast<const void*>(attn_stream_kernel<T, DPV>), smem)) return s; \
+    attn_stream_kernel<T, DPV><<<grid, kStreamThreads, smem, st>>>(a);                     \
+    return check_launch("attn_stream_kernel");                                              \
   }
   switch (dp) {
     SB_ATTN_CASE(16)
@@ -525,8 +564,8 @@ int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask
                          npad, cin, cout, out, workspace, workspace_bytes, stream);
 }
 
-int sb_attn_pair(const void* q, const void* k, const void* v, const uint8_t* pair, const float* table2, int batch,
-                 int heads, int seq, int head_dim, void* out, void* stream) {
+int sb_attn_pair(const void* q, const void* k, const void* v, const uint8_t* pair, const float* table2,
+                 const int32_t* seq_lens, int batch, int heads, int seq, int head_dim, void* out, void* stream) {
   if (!q || !k || !v || !pair || !table2 || !out || batch < 0 || heads <= 0 || seq <= 0)
     return fail(SB_ERR_INVALID_ARG, "attn_pair: bad args");
   if (batch == 0) return SB_OK;
@@ -536,7 +575,7 @@ int sb_attn_pair(const void* q, const void* k, const void* v, const uint8_t* pai
   a.out = out; a.out_pos_stride = a.pos_stride; a.out_head_stride = a.head_stride; a.out_row_stride = head_dim;
   a.B = batch; a.S = seq; a.H = heads; a.D = head_dim; a.ntok = 0;
   a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
-  a.mode = BIAS_PAIR; a.table = table2; a.table_rows = SB_BIAS_ROWS + 1; a.pair = pair;
+  a.mode = BIAS_PAIR; a.table = table2; a.table_rows = SB_BIAS_ROWS + 1; a.pair = pair; a.seq_lens = seq_lens;
   return launch_attention<__half>(a, (cudaStream_t)stream);
 }
 

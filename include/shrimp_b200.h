@@ -161,9 +161,13 @@ int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask
 /* Workspace for sb_hex_conv / sb_hex_conv_ln. */
 int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes);
 /* shrimp::attn_pair (_triton_attn.py:132-171): q, k, v (B, H, S, D) f16 with
- * unit stride on D, pair (B, S, S) uint8, table2 (238, H) f32, out (B, H, S, D). */
+ * unit stride on D, pair (B, S, S) uint8, table2 (238, H) f32 (the op rounds it
+ * to f16: pass f16-representable values for identical results), seq_lens (B)
+ * int32 live lengths or NULL (= S): keys >= seq_lens[b] are skipped and query
+ * rows >= seq_lens[b] are written as zeros (padding; the caller masks them),
+ * out (B, H, S, D). */
 int sb_attn_pair(const void* q, const void* k, const void* v, const uint8_t* pair, const float* table2,
-                 int batch, int heads, int seq, int head_dim, void* out, void* stream);
+                 const int32_t* seq_lens, int batch, int heads, int seq, int head_dim, void* out, void* stream);
 
 /* ---- weight packing ------------------------------------------------------ */
 /* HexNodeConv weight (taps, Cin, Cout) fp32 -> f16 [Cout][Kpad], Kpad =

@@ -209,7 +209,10 @@ def _pack_conv(w, cin_pad=None):
     return out
 
 
-@pytest.mark.parametrize("b,n,cin,cout", [(3, 61, 32, 32), (5, 61, 128, 128), (2, 100, 192, 192), (4, 33, 16, 64)])
+# The last three shapes end in a ragged tile whose valid-row boundary splits an
+# epilogue warp mid-slab (M = 2610, 2610, 2751); they once deadlocked.
+@pytest.mark.parametrize("b,n,cin,cout", [(3, 61, 32, 32), (5, 61, 128, 128), (2, 100, 192, 192), (4, 33, 16, 64),
+                                          (2, 1305, 16, 128), (1, 2610, 128, 128), (3, 917, 32, 64)])
 def test_hex_conv_ops_match_fp32(b, n, cin, cout):
     torch.manual_seed(0)
     x = torch.randn(b, n, cin, device=DEV).half()
@@ -239,21 +242,34 @@ def test_hex_conv_ops_match_fp32(b, n, cin, cout):
     assert (out.float().cpu() - ref).abs().max().item() <= 1e-2
 
 
-@pytest.mark.parametrize("b,h,s,d", [(3, 4, 69, 8), (2, 8, 69, 16), (2, 4, 130, 32), (2, 2, 40, 24), (1, 3, 225, 64)])
-def test_attn_pair_matches_fp32(b, h, s, d):
+@pytest.mark.parametrize("b,h,s,d,jagged", [(3, 4, 69, 8, False), (2, 8, 69, 16, True), (2, 4, 130, 32, False),
+                                              (2, 2, 40, 24, True), (1, 3, 225, 64, False), (3, 12, 225, 16, True)])
+def test_attn_pair_matches_fp32(b, h, s, d, jagged):
     torch.manual_seed(1)
     q = torch.randn(b, h, s, d, device=DEV).half()
     k = torch.randn_like(q)
     v = torch.randn_like(q)
     pair = torch.randint(0, 238, (b, s, s), device=DEV, dtype=torch.uint8)
     pair[:, :, :3] = torch.randint(0, 237, (b, s, 3), device=DEV, dtype=torch.uint8)
-    table = torch.randn(238, h, device=DEV) * 0.5
+    table = (torch.randn(238, h, device=DEV) * 0.5).half().float()
     table[237] = -3e4
-    out = torch.empty_like(q)
+    lens = torch.randint(1, s + 1, (b,), device=DEV, dtype=torch.int32) if jagged else None
+    if jagged:
+        lens[0] = s
+    out = torch.full_like(q, float("nan"))
     _lib.check(_lib.lib().sb_attn_pair(q.data_ptr(), k.data_ptr(), v.data_ptr(), pair.data_ptr(), table.data_ptr(),
-                                       b, h, s, d, out.data_ptr(), stream()), "attn_pair")
+                                       lens.data_ptr() if jagged else None, b, h, s, d, out.data_ptr(), stream()),
+               "attn_pair")
     bias = table[pair.long()].permute(0, 3, 1, 2)
-    ref = torch.softmax(q.float() @ k.float().transpose(-1, -2) / math.sqrt(d) + bias, -1) @ v.float()
+    scores = q.float() @ k.float().transpose(-1, -2) / math.sqrt(d) + bias
+    if jagged:
+        keys = torch.arange(s, device=DEV)
+        scores = scores.masked_fill(keys.view(1, 1, 1, s) >= lens.view(b, 1, 1, 1), float("-inf"))
+    ref = torch.softmax(scores, -1) @ v.float()
+    if jagged:
+        live = torch.arange(s, device=DEV).view(1, 1, s, 1) < lens.view(b, 1, 1, 1)
+        ref = torch.where(live, ref, torch.zeros_like(ref))
+    assert torch.isfinite(out.float()).all()
     assert (out.float() - ref).abs().max().item() <= 5e-3
 
 
@@ -276,16 +292,17 @@ def test_raytap_conv_microbench_matches_oracle():
     assert ((out.float().cpu() - ref).abs() / (1 + ref.abs())).max().item() <= 8e-3
 
 
-def test_offset_attention_microbench_matches_oracle():
+@pytest.mark.parametrize("rows", [217, 817])
+def test_offset_attention_microbench_matches_oracle(rows):
     torch.manual_seed(4)
     b, l, h, d = 16, 61, 8, 32
     q = torch.randn(b, l, h * d, device=DEV).bfloat16()
     k = torch.randn_like(q)
     v = torch.randn_like(q)
-    table = torch.randn(217, h, device=DEV) * 0.5
-    om = torch.randint(0, 217, (l, l), device=DEV, dtype=torch.int32)
+    table = torch.randn(rows, h, device=DEV) * 0.5
+    om = torch.randint(0, rows, (l, l), device=DEV, dtype=torch.int32)
     out = torch.empty_like(q)
-    _lib.check(_lib.lib().sb_offset_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), table.data_ptr(), 217,
+    _lib.check(_lib.lib().sb_offset_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), table.data_ptr(), rows,
                                               om.data_ptr(), b, l, h, d, out.data_ptr(), stream()), "offattn")
     ref = O.offset_bias_attention(q.float().cpu(), k.float().cpu(), v.float().cpu(), table.cpu(), om.cpu(), h)
     torch.cuda.synchronize()
