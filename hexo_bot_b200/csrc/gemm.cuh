@@ -10,7 +10,7 @@
 //
 // Persistent and warp-specialised: one CTA per SM walks 128-row x BN-column
 // output tiles.
-//   warps 0-3  producers. When Cin is a multiple of 64, warp 0 alone feeds the
+//   warps 9-12 producers. When Cin is a multiple of 64, warp 9 alone feeds the
 //              stage ring with TMA: 32 `tile::gather4` loads per 64-wide K
 //              chunk pull the 128 gathered rows straight into the 128-byte
 //              swizzled K-major layout (missing neighbours = out-of-range rows
@@ -20,9 +20,9 @@
 //   warp 8     issues tcgen05.mma (M=128, N=BN, K=16) from one thread into one
 //              of two TMEM accumulators and commits each stage back to the
 //              producers and each finished tile to the epilogue.
-//   warps 4-7  epilogue: one TMEM lane = one output row per thread, so the
-//              LayerNorm statistics need no cross-thread reduction; runs on
-//              accumulator j while the MMA warp fills accumulator j^1.
+//   warps 0-7  epilogue, two warps per TMEM lane quadrant (one output row per
+//              thread, one column half per warp); runs on accumulator j while
+//              the MMA warp fills accumulator j^1.
 // Every mbarrier wait is bounded; a timeout sets a status bit and unwinds.
 #pragma once
 
@@ -103,10 +103,13 @@ struct GemmArgs {
 constexpr int kBlockM = 128;
 constexpr int kChunkK = 64;        // 64 x 16-bit = one 128-byte swizzle row
 constexpr int kTileABytes = kBlockM * 128;
+// Warp roles: 0-7 epilogue (two per TMEM lane quadrant, one per column half),
+// 8 MMA issue, 9-12 producers (TMA: warp 9 alone).
+constexpr int kEpiWarps = 8;
+constexpr int kMmaWarp = kEpiWarps;
+constexpr int kProducerWarp0 = kMmaWarp + 1;
 constexpr int kProducerWarps = 4;
-constexpr int kEpiWarps = 4;
-constexpr int kMmaWarp = kProducerWarps + kEpiWarps;
-constexpr int kGemmThreads = (kMmaWarp + 1) * 32;  // 288
+constexpr int kGemmThreads = (kProducerWarp0 + kProducerWarps) * 32;  // 416
 constexpr int kMaxTaps = 19;
 constexpr int kMaxStages = 8;
 
@@ -182,22 +185,23 @@ __device__ __forceinline__ void stats_merge(float& cnt, float& mean, float& m2, 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
 
 // ---- epilogue ---------------------------------------------------------------
-// Each epilogue warp owns 32 accumulator rows (one TMEM lane per thread) and
-// walks them in 32-column slabs: values are computed row-per-thread from TMEM
-// and the shared-memory copies of the epilogue vectors, staged in swizzled
-// shared memory, and moved to / from global memory with coalesced accesses
-// (8 lanes per 128-byte fp32 row slab, 4 lanes per 64-byte 16-bit row slab).
+// Eight warps: warp w reads TMEM lane quadrant w % 4 (32 accumulator rows, one
+// row per thread) and column half w / 4 of the tile. Row-wise statistics
+// (LayerNorm A / B, the policy-head dot product) are combined with the partner
+// warp of the same quadrant through a small shared-memory exchange and a
+// 64-thread named barrier. Values go from TMEM to registers 32 columns at a
+// time and straight to / from global memory as 16-byte row pieces; every
+// lane-dependent access is a single predicated instruction, so the warp stays
+// converged for the .sync.aligned TMEM loads.
 
-constexpr int kSlab = 32;                       // columns per slab
-constexpr int kStage32Bytes = 32 * kSlab * 4;   // 4 KB per warp
-constexpr int kStage16Bytes = 32 * kSlab * 2;   // 2 KB per warp
 constexpr int kEpiVecFloats = 1024 + 6 * 256;   // bias (n_total) + six N-vectors
-constexpr int kEpiSmemBytes = kEpiWarps * (kStage32Bytes + kStage16Bytes) + kEpiVecFloats * 4;
+constexpr int kEpiXchBytes = 4 * 2 * 32 * 16;    // [quadrant][half][row] float4
+constexpr int kEpiSmemBytes = kEpiVecFloats * 4 + kEpiXchBytes;
 
 __host__ __device__ constexpr int gemm_smem_bytes(int bn, int stages, int taps) {
   return 1024 + stages * gemm_stage_bytes(bn) + gemm_gidx_bytes(taps) + kEpiSmemBytes + 8 * (2 * stages + 4) + 16;
 }
-// Stages that fit next to the gather-index double buffer and epilogue staging.
+// Stages that fit next to the gather-index double buffer and the epilogue data.
 __host__ __device__ constexpr int gemm_stages(int bn, int taps) {
   int s = kMaxStages;
   while (s > 2 && gemm_smem_bytes(bn, s, taps) > 227 * 1024) --s;
@@ -205,217 +209,285 @@ __host__ __device__ constexpr int gemm_stages(int bn, int taps) {
 }
 
 struct EpiVecs {
-  float* bias;  // [n_total]
-  float* lnaw;
-  float* lnab;
-  float* lnbw;
-  float* lnbb;
-  float* gamma;
-  float* headw;
+  const float* bias;  // [n_total]
+  const float* lnaw;
+  const float* lnab;
+  const float* lnbw;
+  const float* lnbb;
+  const float* gamma;
+  const float* headw;
 };
 
-// fp32 slab staging: row r, 16-byte piece p (4 floats) at r*128 + ((p ^ (r & 7)) << 4)
-__device__ __forceinline__ uint32_t st32_off(int r, int p) { return r * 128 + ((p ^ (r & 7)) << 4); }
-// 16-bit slab staging: row r, piece p (8 halves) at r*64 + ((p ^ ((r >> 1) & 3)) << 4)
-__device__ __forceinline__ uint32_t st16_off(int r, int p) { return r * 64 + ((p ^ ((r >> 1) & 3)) << 4); }
+// 32 TMEM columns (two x16 loads, one wait) of this thread's row.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  __syncwarp();
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr + 16));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
 
-// Coalesced copies of a 32-row x 32-float slab between global rows and the
-// staging: 8 lanes per row, rows 4 i + lane / 8.
-__device__ __forceinline__ void slab32_global_to_stage(uint8_t* st, const float* base, long long ld, int c0,
-                                                       const long long (&rows)[8], const bool (&ok)[8], int lane) {
+// TMEM -> registers for `w` (16 or 32) columns starting at column c.
+template <int W>
+__device__ __forceinline__ void tmem_ldw(uint32_t taddr, float (&v)[32]) {
+  if (W == 32) {
+    tmem_ld32(taddr, v);
+  } else {
+    float t[16];
+    tmem_ld16(taddr, t);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = 4 * i + (lane >> 3), p = lane & 7;
-    *reinterpret_cast<uint4*>(st + st32_off(r, p)) = ld_global_v4_if(base + rows[i] * ld + c0 + 4 * p, ok[i]);
+    for (int i = 0; i < 16; ++i) v[i] = t[i];
   }
 }
-__device__ __forceinline__ void slab32_stage_to_global(const uint8_t* st, float* base, long long ld, int c0,
-                                                       const long long (&rows)[8], const bool (&ok)[8], int lane) {
+
+template <int W>
+__device__ __forceinline__ void ld_vec(const float* p, float (&v)[32]) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = 4 * i + (lane >> 3), p = lane & 7;
-    st_global_v4_if(base + rows[i] * ld + c0 + 4 * p, *reinterpret_cast<const uint4*>(st + st32_off(r, p)), ok[i]);
+  for (int i = 0; i < W / 4; ++i) {
+    const float4 f = reinterpret_cast<const float4*>(p)[i];
+    v[4 * i] = f.x;
+    v[4 * i + 1] = f.y;
+    v[4 * i + 2] = f.z;
+    v[4 * i + 3] = f.w;
   }
 }
-template <typename T>
-__device__ __forceinline__ void slab16_store(const float (&v)[kSlab], uint8_t* st16, void* out, long long ld,
-                                             int c0, const long long (&r16)[4], const bool (&ok)[4], int lane) {
+
+template <int W>
+__device__ __forceinline__ void stats_merge_w(float& cnt, float& mean, float& m2, const float (&v)[32]) {
+  float a[16];
 #pragma unroll
-  for (int p = 0; p < kSlab / 8; ++p) {
+  for (int i = 0; i < 16; ++i) a[i] = v[i];
+  stats_merge(cnt, mean, m2, a);
+  if (W == 32) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] = v[16 + i];
+    stats_merge(cnt, mean, m2, a);
+  }
+}
+
+// Combine (cnt, mean, m2) with the partner warp's (Chan), always in the
+// order (half 0, half 1) so both warps get bit-identical statistics.
+__device__ __forceinline__ void stats_combine(float& cnt, float& mean, float& m2, float4* xme, const float4* xother,
+                                              int bar_id, int half) {
+  *xme = make_float4(cnt, mean, m2, 0.f);
+  asm volatile("bar.sync %0, 64;\n" ::"r"(bar_id) : "memory");
+  const float4 o = *xother;
+  asm volatile("bar.sync %0, 64;\n" ::"r"(bar_id) : "memory");
+  const float c0 = half ? o.x : cnt, u0 = half ? o.y : mean, q0 = half ? o.z : m2;
+  const float c1 = half ? cnt : o.x, u1 = half ? mean : o.y, q1 = half ? m2 : o.z;
+  const float tot = c0 + c1;
+  const float delta = u1 - u0;
+  const float w = tot > 0.f ? c1 / tot : 0.f;
+  m2 = q0 + q1 + delta * delta * c0 * w;
+  mean = fmaf(delta, w, u0);
+  cnt = tot;
+}
+
+// fp32 row piece: 4 x 16-byte predicated stores / loads of W/4 ... columns.
+template <int W>
+__device__ __forceinline__ void st_row32(float* p, const float (&v)[32], bool ok) {
+#pragma unroll
+  for (int i = 0; i < W / 4; ++i)
+    st_global_v4_if(p + 4 * i, make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]),
+                                          __float_as_uint(v[4 * i + 2]), __float_as_uint(v[4 * i + 3])),
+                    ok);
+}
+template <int W>
+__device__ __forceinline__ void ld_row32(const float* p, float (&v)[32], bool ok) {
+#pragma unroll
+  for (int i = 0; i < W / 4; ++i) {
+    const uint4 u = ld_global_v4_if(p + 4 * i, ok);
+    v[4 * i] = __uint_as_float(u.x);
+    v[4 * i + 1] = __uint_as_float(u.y);
+    v[4 * i + 2] = __uint_as_float(u.z);
+    v[4 * i + 3] = __uint_as_float(u.w);
+  }
+}
+template <typename T, int W>
+__device__ __forceinline__ void st_row16(void* p, const float (&v)[32], bool ok) {
+#pragma unroll
+  for (int i = 0; i < W / 8; ++i) {
     uint4 u;
     T* h = reinterpret_cast<T*>(&u);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(v[8 * p + e]);
-    *reinterpret_cast<uint4*>(st16 + st16_off(lane, p)) = u;
+    for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(v[8 * i + e]);
+    st_global_v4_if(reinterpret_cast<T*>(p) + 8 * i, u, ok);
   }
-  __syncwarp();
+}
+template <typename T, int W>
+__device__ __forceinline__ void ld_row16(const void* p, float (&v)[32], bool ok) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = 8 * i + (lane >> 2), p = lane & 3;
-    st_global_v4_if(reinterpret_cast<T*>(out) + r16[i] * ld + c0 + 8 * p,
-                    *reinterpret_cast<const uint4*>(st16 + st16_off(r, p)), ok[i]);
+  for (int i = 0; i < W / 8; ++i) {
+    const uint4 u = ld_global_v4_if(reinterpret_cast<const T*>(p) + 8 * i, ok);
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[8 * i + e] = to_f32<T>(h[e]);
   }
-  __syncwarp();
+}
+
+// Per-thread row context of one tile.
+struct EpiRow {
+  bool valid;       // GEMM row < M
+  int mc;           // GEMM row, clamped to M - 1
+  long long orow;   // output row
+  float mk;         // row mask (EPI_MASK / EPI_HEAD)
+  bool lnb_row;     // LayerNorm B applies to this row
+};
+
+// Main pass over one chunk of W columns [c, c + W) of the tile (tile-local
+// column c, global column n0 + c).
+template <typename T, int W>
+__device__ __forceinline__ void epi_chunk_main(const GemmArgs& a, const EpiVecs& ev, const EpiRow& r, int n0, int c,
+                                               uint32_t tcol, float mean_a, float rstd_a, float& head,
+                                               float& cntb, float& meanb, float& m2b) {
+  const int fl = a.flags;
+  float v[32], t[32];
+  tmem_ldw<W>(tcol, v);
+  ld_vec<W>(ev.bias + n0 + c, t);
+#pragma unroll
+  for (int i = 0; i < W; ++i) v[i] += t[i];
+  if (fl & EPI_LN_A) {
+    float w[32];
+    ld_vec<W>(ev.lnaw + c, w);
+    ld_vec<W>(ev.lnab + c, t);
+#pragma unroll
+    for (int i = 0; i < W; ++i) v[i] = fmaf((v[i] - mean_a) * rstd_a, w[i], t[i]);
+  }
+  if (fl & EPI_RELU) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) v[i] = fmaxf(v[i], 0.f);
+  }
+  if (fl & EPI_GELU) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) v[i] = gelu_erf(v[i]);
+  }
+  if (fl & EPI_HEAD) {
+    ld_vec<W>(ev.headw + c, t);
+#pragma unroll
+    for (int i = 0; i < W; ++i) head = fmaf(fmaxf(v[i], 0.f), t[i], head);
+    return;
+  }
+  if (fl & EPI_MASK) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) v[i] *= r.mk;
+  }
+  if (fl & EPI_RESID) {
+    float x[32];
+    ld_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, x, r.valid);
+    ld_vec<W>(ev.gamma + c, t);
+#pragma unroll
+    for (int i = 0; i < W; ++i) v[i] = fmaf(v[i], t[i], x[i]);
+  }
+  if (fl & EPI_POST_RELU) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) v[i] = fmaxf(v[i], 0.f);
+  }
+  if (fl & EPI_RES16) {
+    ld_row16<T, W>(reinterpret_cast<const T*>(a.res16) + r.orow * a.ldr16 + n0 + c, t, true);
+#pragma unroll
+    for (int i = 0; i < W; ++i) v[i] = fmaxf(v[i] + t[i], 0.f);
+  }
+  if (fl & EPI_LN_B) stats_merge_w<W>(cntb, meanb, m2b, v);
+  if (fl & (EPI_RESID | EPI_OUT32)) st_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, v, r.valid);
+  if (fl & EPI_OUT16) st_row16<T, W>(reinterpret_cast<T*>(a.out16) + r.orow * a.ld16 + n0 + c, v,
+                                     r.valid && !r.lnb_row);
+}
+
+// LayerNorm B over the stored fp32 row (re-read: this thread wrote it).
+template <typename T, int W>
+__device__ __forceinline__ void epi_chunk_lnb(const GemmArgs& a, const EpiVecs& ev, const EpiRow& r, int n0, int c,
+                                              float meanb, float rstd_b) {
+  float v[32], w[32], t[32];
+  ld_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, v, r.valid);
+  ld_vec<W>(ev.lnbw + c, w);
+  ld_vec<W>(ev.lnbb + c, t);
+#pragma unroll
+  for (int i = 0; i < W; ++i) v[i] = fmaf((v[i] - meanb) * rstd_b, w[i], t[i]);
+  const bool okb = r.valid && r.lnb_row;
+  if (a.flags & EPI_OUT32B) st_row32<W>(a.out32b + r.orow * a.ld32b + n0 + c, v, okb);
+  if (a.flags & EPI_OUT16) st_row16<T, W>(reinterpret_cast<T*>(a.out16) + r.orow * a.ld16 + n0 + c, v, okb);
 }
 
 template <typename T>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& ev, uint8_t* st32, uint8_t* st16,
-                                              int m_first, int n0, uint32_t tbase, int lane) {
-  // No branch below depends on the lane: the tcgen05.ld / wait::ld of this
-  // function are .sync.aligned and must run with the warp converged, so rows
-  // past M are clamped onto row M-1 for every load and only the stores are
-  // predicated.
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& ev, float4* xch, int bar_id,
+                                              int half, int m_first, int n0, uint32_t tbase, int lane) {
+  // No branch below depends on the lane: rows past M are clamped onto row
+  // M-1 for every load and only the stores are predicated.
+  EpiRow r;
   const int m = m_first + lane;
-  const bool valid = m < a.M;
-  const int mc = valid ? m : a.M - 1;
-  const long long orow =
-      (a.gidx && a.orow_from_gidx) ? (long long)__ldg(a.gidx + (long long)mc * a.taps) : (long long)mc;
+  r.valid = m < a.M;
+  r.mc = r.valid ? m : a.M - 1;
+  r.orow = (a.gidx && a.orow_from_gidx) ? (long long)__ldg(a.gidx + (long long)r.mc * a.taps) : (long long)r.mc;
   const int fl = a.flags;
-  const float mk = ((fl & (EPI_MASK | EPI_HEAD)) && a.rowmask) ? __ldg(a.rowmask + orow) : 1.f;
-  bool lnb_row = (fl & EPI_LN_B) != 0;
-  if (fl & EPI_LNB_TOKENS) lnb_row = lnb_row && valid && (orow % a.seq_len) < a.ntok;
+  r.mk = ((fl & (EPI_MASK | EPI_HEAD)) && a.rowmask) ? __ldg(a.rowmask + r.orow) : 1.f;
+  r.lnb_row = (fl & EPI_LN_B) != 0;
+  if (fl & EPI_LNB_TOKENS) r.lnb_row = r.lnb_row && r.valid && (r.orow % a.seq_len) < a.ntok;
 
-  long long r32[8];  // fp32 pattern rows 4 i + lane / 8
-  bool ok32[8], okb[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int src = 4 * i + (lane >> 3);
-    // every lane executes every shuffle (no short-circuit around a
-    // full-mask __shfl_sync: lanes that skipped it would leave the others
-    // waiting forever)
-    r32[i] = __shfl_sync(0xffffffffu, orow, src);
-    ok32[i] = __shfl_sync(0xffffffffu, (int)valid, src) != 0;
-    const bool lb = __shfl_sync(0xffffffffu, (int)lnb_row, src) != 0;
-    okb[i] = ok32[i] && lb;
-  }
-  long long r16[4];  // 16-bit pattern rows 8 i + lane / 4
-  bool raw16[4], lnb16[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int src = 8 * i + (lane >> 2);
-    r16[i] = __shfl_sync(0xffffffffu, orow, src);
-    const bool ok = __shfl_sync(0xffffffffu, (int)valid, src) != 0;
-    const bool lb = __shfl_sync(0xffffffffu, (int)lnb_row, src) != 0;
-    raw16[i] = ok && !lb;
-    lnb16[i] = ok && lb;
-  }
+  const int hw = a.bn >> 1;                     // columns per half
+  const int c_lo = half * hw, c_hi = c_lo + hw;  // tile-local columns of this warp
+  float4* xme = xch + half * 32 + lane;
+  const float4* xot = xch + (half ^ 1) * 32 + lane;
 
-  const int nslab = a.bn / kSlab;
   float mean_a = 0.f, rstd_a = 1.f;
   if (fl & EPI_LN_A) {
     float cnt = 0.f, mean = 0.f, m2 = 0.f;
-    for (int ch = 0; ch < a.bn / 16; ++ch) {
-      float v[16];
-      tmem_ld16(tbase + ch * 16, v);
+    int c = c_lo;
+    for (; c + 32 <= c_hi; c += 32) {
+      float v[32], t[32];
+      tmem_ldw<32>(tbase + c, v);
+      ld_vec<32>(ev.bias + n0 + c, t);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] += ev.bias[n0 + ch * 16 + i];
-      stats_merge(cnt, mean, m2, v);
+      for (int i = 0; i < 32; ++i) v[i] += t[i];
+      stats_merge_w<32>(cnt, mean, m2, v);
     }
+    if (c < c_hi) {
+      float v[32], t[32];
+      tmem_ldw<16>(tbase + c, v);
+      ld_vec<16>(ev.bias + n0 + c, t);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] += t[i];
+      stats_merge_w<16>(cnt, mean, m2, v);
+    }
+    stats_combine(cnt, mean, m2, xme, xot, bar_id, half);
     mean_a = mean;
     rstd_a = rsqrtf(m2 / cnt + a.eps);
   }
 
-  float cntb = 0.f, meanb = 0.f, m2b = 0.f;
-  float head = 0.f;
-  const bool need32 = (fl & (EPI_RESID | EPI_OUT32)) != 0;
-  for (int sl = 0; sl < nslab; ++sl) {
-    const int c0 = sl * kSlab;
-    if (fl & EPI_RESID) {
-      slab32_global_to_stage(st32, a.out32, a.ld32, n0 + c0, r32, ok32, lane);
-      __syncwarp();
-    }
-    float lo[16], hi[16];
-    tmem_ld16(tbase + c0, lo);
-    tmem_ld16(tbase + c0 + 16, hi);
-    float v[kSlab];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      v[i] = lo[i];
-      v[16 + i] = hi[i];
-    }
-#pragma unroll
-    for (int i = 0; i < kSlab; ++i) {
-      float x = v[i] + ev.bias[n0 + c0 + i];
-      if (fl & EPI_LN_A) x = fmaf((x - mean_a) * rstd_a, ev.lnaw[c0 + i], ev.lnab[c0 + i]);
-      if (fl & EPI_RELU) x = fmaxf(x, 0.f);
-      if (fl & EPI_GELU) x = gelu_erf(x);
-      v[i] = x;
-    }
-    if (fl & EPI_HEAD) {
-#pragma unroll
-      for (int i = 0; i < kSlab; ++i) head = fmaf(fmaxf(v[i], 0.f), ev.headw[c0 + i], head);
-      continue;
-    }
-#pragma unroll
-    for (int i = 0; i < kSlab; ++i) {
-      float x = v[i];
-      if (fl & EPI_MASK) x *= mk;
-      if (fl & EPI_RESID) {
-        const float xr = reinterpret_cast<const float*>(st32 + st32_off(lane, i >> 2))[i & 3];
-        x = fmaf(x, ev.gamma[c0 + i], xr);
-      }
-      if (fl & EPI_POST_RELU) x = fmaxf(x, 0.f);
-      v[i] = x;
-    }
-    if (fl & EPI_RES16) {
-      float q0[16], q1[16];
-      load16<T>(a.res16, orow * a.ldr16 + n0 + c0, q0);
-      load16<T>(a.res16, orow * a.ldr16 + n0 + c0 + 16, q1);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        v[i] = fmaxf(v[i] + q0[i], 0.f);
-        v[16 + i] = fmaxf(v[16 + i] + q1[i], 0.f);
-      }
-    }
-    if (fl & EPI_LN_B) {  // statistics on every lane (uniform branch); used where lnb_row
-      float s0[16], s1[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        s0[i] = v[i];
-        s1[i] = v[16 + i];
-      }
-      stats_merge(cntb, meanb, m2b, s0);
-      stats_merge(cntb, meanb, m2b, s1);
-    }
-    if (need32) {
-      __syncwarp();
-#pragma unroll
-      for (int p = 0; p < kSlab / 4; ++p)
-        *reinterpret_cast<float4*>(st32 + st32_off(lane, p)) =
-            make_float4(v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
-      __syncwarp();
-      slab32_stage_to_global(st32, a.out32, a.ld32, n0 + c0, r32, ok32, lane);
-      __syncwarp();
-    }
-    if (fl & EPI_OUT16) slab16_store<T>(v, st16, a.out16, a.ld16, n0 + c0, r16, raw16, lane);
+  float head = 0.f, cntb = 0.f, meanb = 0.f, m2b = 0.f;
+  {
+    int c = c_lo;
+    for (; c + 32 <= c_hi; c += 32)
+      epi_chunk_main<T, 32>(a, ev, r, n0, c, tbase + c, mean_a, rstd_a, head, cntb, meanb, m2b);
+    if (c < c_hi) epi_chunk_main<T, 16>(a, ev, r, n0, c, tbase + c, mean_a, rstd_a, head, cntb, meanb, m2b);
   }
-  if ((fl & EPI_HEAD) && a.head_out) st_global_f32_if(a.head_out + mc, mk * (head + a.head_b), valid);
 
-  // pass 3: LayerNorm_b of the stored fp32 rows (re-read through the staging)
-  if ((fl & EPI_LN_B) && __any_sync(0xffffffffu, lnb_row)) {
-    const float rstd_b = lnb_row ? rsqrtf(m2b / cntb + a.eps) : 1.f;
-    for (int sl = 0; sl < nslab; ++sl) {
-      const int c0 = sl * kSlab;
-      slab32_global_to_stage(st32, a.out32, a.ld32, n0 + c0, r32, ok32, lane);
-      __syncwarp();
-      float v[kSlab];
-#pragma unroll
-      for (int i = 0; i < kSlab; ++i) {
-        const float x = reinterpret_cast<const float*>(st32 + st32_off(lane, i >> 2))[i & 3];
-        v[i] = fmaf((x - meanb) * rstd_b, ev.lnbw[c0 + i], ev.lnbb[c0 + i]);
-      }
-      __syncwarp();
-      if (fl & EPI_OUT32B) {
-#pragma unroll
-        for (int p = 0; p < kSlab / 4; ++p)
-          *reinterpret_cast<float4*>(st32 + st32_off(lane, p)) =
-              make_float4(v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
-        __syncwarp();
-        slab32_stage_to_global(st32, a.out32b, a.ld32b, n0 + c0, r32, okb, lane);
-        __syncwarp();
-      }
-      if (fl & EPI_OUT16) slab16_store<T>(v, st16, a.out16, a.ld16, n0 + c0, r16, lnb16, lane);
-    }
+  if (fl & EPI_HEAD) {
+    *xme = make_float4(head, 0.f, 0.f, 0.f);
+    asm volatile("bar.sync %0, 64;\n" ::"r"(bar_id) : "memory");
+    head = half ? xot->x + head : head + xot->x;
+    asm volatile("bar.sync %0, 64;\n" ::"r"(bar_id) : "memory");
+    if (a.head_out) st_global_f32_if(a.head_out + r.mc, r.mk * (head + a.head_b), r.valid && half == 0);
+  }
+
+  if (fl & EPI_LN_B) {
+    stats_combine(cntb, meanb, m2b, xme, xot, bar_id, half);
+    const float rstd_b = rsqrtf(m2b / fmaxf(cntb, 1.f) + a.eps);
+    // the fp32 row pieces this thread stored above must be visible to its own re-read
+    int c = c_lo;
+    for (; c + 32 <= c_hi; c += 32) epi_chunk_lnb<T, 32>(a, ev, r, n0, c, meanb, rstd_b);
+    if (c < c_hi) epi_chunk_lnb<T, 16>(a, ev, r, n0, c, meanb, rstd_b);
   }
 }
 
@@ -477,7 +549,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t gidx_off = S * stage_bytes;
   int32_t* gsm = reinterpret_cast<int32_t*>(gbase + gidx_off);        // [2][128 * taps]
   const uint32_t epi_off = gidx_off + gemm_gidx_bytes(a.taps);
-  uint8_t* epi_smem = gbase + epi_off;                                 // staging + vectors
+  float* vecs = reinterpret_cast<float*>(gbase + epi_off);             // epilogue vectors
+  float4* xch_all = reinterpret_cast<float4*>(gbase + epi_off + kEpiVecFloats * 4);  // [4][2][32]
   const uint32_t bar0 = base + epi_off + kEpiSmemBytes;
   const uint32_t full_bar = bar0;                 // [S]
   const uint32_t empty_bar = bar0 + 8 * S;        // [S]
@@ -521,11 +594,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot_ptr;
   bool ok = true;
 
-  if (warp < kProducerWarps) {
+  if (warp >= kProducerWarp0) {
     // ------------------------------------------------------------ producers
-    const int pt = tid;  // 0..127
-    if (tma && warp != 0) {
-      // only warp 0 issues TMA
+    const int pt = tid - kProducerWarp0 * 32;  // 0..127
+    if (tma && warp != kProducerWarp0) {
+      // only the first producer warp issues TMA
     } else {
       uint32_t it = 0;
       int j = 0;
@@ -655,26 +728,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - kProducerWarps;  // == warp % 4: TMEM lanes [32 ew, 32 ew + 32)
-    uint8_t* st32 = epi_smem + ew * (kStage32Bytes + kStage16Bytes);
-    uint8_t* st16 = st32 + kStage32Bytes;
-    float* vecs = reinterpret_cast<float*>(epi_smem + kEpiWarps * (kStage32Bytes + kStage16Bytes));
-    EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768, vecs + 1024 + 1024,
-               vecs + 1024 + 1280};
+    const int quad = warp & 3;   // TMEM lanes [32 quad, 32 quad + 32)
+    const int half = warp >> 2;  // column half of the tile
+    const int bar_id = 3 + quad; // named barrier of the quadrant's warp pair
+    float4* xch = xch_all + quad * 64;
     {
-      const int et = tid - kProducerWarps * 32;  // 0..127
-      const bool rowwise = a.bn == a.n_total;    // LN / head vectors only exist then
-      for (int i = et; i < a.n_total && i < 1024; i += kEpiWarps * 32) ev.bias[i] = __ldg(a.bias + i);
-      for (int i = et; i < a.bn && rowwise; i += kEpiWarps * 32) {
-        ev.lnaw[i] = a.ln_a_w ? __ldg(a.ln_a_w + i) : 0.f;
-        ev.lnab[i] = a.ln_a_b ? __ldg(a.ln_a_b + i) : 0.f;
-        ev.lnbw[i] = a.ln_b_w ? __ldg(a.ln_b_w + i) : 0.f;
-        ev.lnbb[i] = a.ln_b_b ? __ldg(a.ln_b_b + i) : 0.f;
-        ev.headw[i] = a.head_w ? __ldg(a.head_w + i) : 0.f;
-        ev.gamma[i] = a.gamma ? __ldg(a.gamma + i) : 0.f;
+      float* bias_s = vecs;
+      float* lnaw = vecs + 1024;
+      const bool rowwise = a.bn == a.n_total;  // LN / head vectors only exist then
+      for (int i = tid; i < a.n_total && i < 1024; i += kEpiWarps * 32) bias_s[i] = __ldg(a.bias + i);
+      for (int i = tid; i < a.bn && rowwise; i += kEpiWarps * 32) {
+        lnaw[i] = a.ln_a_w ? __ldg(a.ln_a_w + i) : 0.f;
+        lnaw[256 + i] = a.ln_a_b ? __ldg(a.ln_a_b + i) : 0.f;
+        lnaw[512 + i] = a.ln_b_w ? __ldg(a.ln_b_w + i) : 0.f;
+        lnaw[768 + i] = a.ln_b_b ? __ldg(a.ln_b_b + i) : 0.f;
+        lnaw[1024 + i] = a.gamma ? __ldg(a.gamma + i) : 0.f;
+        lnaw[1280 + i] = a.head_w ? __ldg(a.head_w + i) : 0.f;
       }
-      asm volatile("bar.sync 2, 128;\n" ::: "memory");
+      asm volatile("bar.sync 2, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
     }
+    const EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768,
+                     vecs + 1024 + 1024, vecs + 1024 + 1280};
     int j = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
       const int nt = t % n_tiles, mt = t / n_tiles;
@@ -683,11 +757,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // .sync.aligned TMEM loads of the epilogue)
       const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (j >> 1) & 1);
       ok = __all_sync(0xffffffffu, got) != 0;
+      // Both warps of a quadrant pair must agree on running the tile (they
+      // exchange row statistics through named barriers): AND across the pair.
+      ok = bar_red_and(bar_id, 64, ok);
       if (!ok && lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_EPILOGUE);
       tc_fence_after();
       if (ok) {
-        const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(ew * 32) << 16);
-        epilogue_tile<T>(a, ev, st32, st16, mt * kBlockM + ew * 32, nt * a.bn, trow, lane);
+        const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
+        epilogue_tile<T>(a, ev, xch, bar_id, half, mt * kBlockM + quad * 32, nt * a.bn, trow, lane);
       }
       tc_fence_before();
       __syncwarp();

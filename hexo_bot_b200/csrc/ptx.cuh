@@ -199,6 +199,18 @@ __host__ __device__ constexpr uint32_t mma_idesc(int n, bool is_bf16) {
 }
 
 
+// Named barrier over `nthreads` threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool bar_red_and(int id, int nthreads, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\t"
+      "bar.red.and.pred b, %2, %3, a;\n\tselp.u32 %0, 1, 0, b;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)p), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // ---- predicated global accesses ------------------------------------------------
 // Lane-dependent stores / loads as single predicated instructions, so code
 // around tcgen05 .sync.aligned instructions never branches on the lane.
