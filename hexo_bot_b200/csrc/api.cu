@@ -14,6 +14,7 @@
 #include "attention.cuh"
 #include "aux.cuh"
 #include "gemm.cuh"
+#include "conv_ts.cuh"
 
 namespace sb {
 namespace {
@@ -177,6 +178,52 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
     fprintf(stderr, "[sb] gemm M=%d N=%d bn=%d kpad=%d taps=%d cin=%d tma=%d stages=%d smem=%d grid=%d flags=%d\n",
             a.M, a.n_total, a.bn, a.kpad, a.taps, a.cin, a.use_tma, stages, smem, grid, a.flags);
   return check_launch("gemm_ws_kernel");
+}
+
+// Position-windowed 7-tap conv (conv_ts_kernel) when the shape allows it:
+// C = Cin = Cout a multiple of 64 up to 256, whole positions of <= 128 cells
+// per 128-row tile, a window of <= 256 X rows. Returns 1 when not eligible
+// (the caller then runs the gather-GEMM), else an sb_status.
+template <typename T>
+int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) {
+  const int C = a.n_total;
+  if (a.taps != 7 || !a.gidx || a.cin != C || C % 64 || C > 256 || cells <= 0 || cells > kBlockM || xrows < cells)
+    return 1;
+  if (a.lda != C || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16 || producer_mode() == 1) return 1;
+  int ppt = kBlockM / cells;
+  while (ppt > 1 && ppt * xrows > 256) --ppt;
+  if (ppt * xrows > 256) return 1;
+  const int win_rows = ppt * xrows;
+  const int stages = conv_ts_stages(C, win_rows);
+  const int smem = conv_ts_smem_bytes(C, stages, win_rows);
+  if (smem > 227 * 1024) return 1;
+  if (a.M <= 0 || npos <= 0) return SB_OK;
+  a.bn = C;
+  a.kpad = 7 * C;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap mx, mw;
+  memset(&mx, 0, sizeof(mx));
+  memset(&mw, 0, sizeof(mw));
+  if (int s = make_tmap(&mx, a.A, bf16, C, (long long)npos * xrows, C, win_rows)) return s;
+  if (int s = make_tmap(&mw, a.Bw, bf16, a.kpad, C, a.kpad, C)) return s;
+  if (int s = ensure_smem(reinterpret_cast<const void*>(conv_ts_kernel<T>), smem)) return s;
+  ConvTsGeom geo{ppt, cells, xrows, npos};
+  const int tiles = (npos + ppt - 1) / ppt;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  conv_ts_kernel<T><<<grid, kConvThreads, smem, st>>>(a, geo, mx, mw, stages);
+  if (sync_debug())
+    fprintf(stderr, "[sb] conv_ts M=%d C=%d ppt=%d win=%d stages=%d smem=%d grid=%d flags=%d\n", a.M, C, ppt,
+            win_rows, stages, smem, grid, a.flags);
+  return check_launch("conv_ts_kernel");
+}
+
+// 7-tap conv over whole positions: the windowed kernel when eligible, else
+// the gather-GEMM.
+template <typename T>
+int launch_conv(const GemmArgs& a, int npos, int cells, int xrows, cudaStream_t st) {
+  const int r = launch_conv_ts<T>(a, npos, cells, xrows, st);
+  if (r != 1) return r;
+  return launch_gemm<T>(a, st);
 }
 
 template <typename T>
@@ -416,7 +463,7 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
       g1.ln_a_w = w.ln1_w; g1.ln_a_b = w.ln1_b;
       g1.flags = EPI_LN_A | EPI_RELU | EPI_MASK | EPI_OUT16;
       g1.out16 = y16; g1.ld16 = C;
-      if (int s = launch_gemm<__half>(g1, st)) return s;
+      if (int s = launch_conv<__half>(g1, B, npad, S, st)) return s;
       GemmArgs g2 = conv_args(y16, w.w2, w.b2);
       g2.ln_a_w = w.ln2_w; g2.ln_a_b = w.ln2_b; g2.gamma = w.gamma;
       g2.flags = EPI_LN_A | EPI_MASK | EPI_RESID | EPI_POST_RELU | EPI_OUT32 | EPI_OUT16;
@@ -426,7 +473,7 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
         g2.flags |= EPI_LN_B;
         g2.ln_b_w = net->attn[na].ln1_w; g2.ln_b_b = net->attn[na].ln1_b;
       }
-      if (int s = launch_gemm<__half>(g2, st)) return s;
+      if (int s = launch_conv<__half>(g2, B, npad, S, st)) return s;
     } else {
       const sb_attn_block_weights& w = net->attn[ai];
       // q | k | v projections of LN1(seq) (model.py:448-455)
@@ -474,7 +521,7 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
   {
     GemmArgs g = conv_args(xa16, net->policy_conv_w, net->policy_conv_b);
     g.flags = EPI_HEAD; g.head_w = net->policy_head_w; g.head_b = net->policy_head_b; g.head_out = out->policy;
-    if (int s = launch_gemm<__half>(g, st)) return s;
+    if (int s = launch_conv<__half>(g, B, npad, S, st)) return s;
   }
   // value (+ moves-left) heads and decode (model.py:984-1003, losses.py:40-61)
   {
@@ -546,7 +593,7 @@ static int hex_conv_common(const void* x, const int32_t* gather_idx, const uint8
   g.Bw = w; g.kpad = round_up(7 * cin, kChunkK); g.n_total = cout; g.bn = 0;
   g.bias = bias; g.ln_a_w = ln_w; g.ln_a_b = ln_b; g.eps = eps; g.rowmask = rm;
   g.flags = flags | EPI_MASK | EPI_OUT16; g.out16 = out; g.ld16 = cout;
-  return launch_gemm<__half>(g, st);
+  return launch_conv<__half>(g, batch, npad, npad, st);
 }
 
 int sb_hex_conv(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w, const float* bias,

@@ -1,0 +1,315 @@
+// HexNodeConv (7 taps) for short positions, with the A operand built on chip.
+//
+//   out[m, :] = epilogue( sum_t X[src(m, t), :] @ W_t )      (model.py:346-370)
+//
+// Tiles are aligned to positions: one tile = `ppt` whole positions
+// (ppt * cells <= 128 output rows; 2 positions of 61 cells in the disk
+// regime). The rows of those positions (the "window": ppt * rows-per-position
+// rows of X, contiguous in memory) arrive in shared memory with one 2D TMA
+// load per 64-column box, so every X row crosses from L2 once per tile instead
+// of once per tap. Four A-builder warps (one per TMEM lane quadrant, one
+// output row per thread) gather each 64-wide K chunk of their row's 7 taps
+// from the window and store it into TMEM; the MMA warp runs tcgen05.mma with
+// A from TMEM and the weight chunk (streamed through a TMA ring) from shared
+// memory, so shared-memory bandwidth is spent on the weights and the gather
+// reads only. The epilogue is the eight-warp epilogue of gemm_ws_kernel.
+//
+// Warp roles (480 threads): 0-7 epilogue, 8 MMA issue, 9 weight producer,
+// 10-13 A builders, 14 window producer.
+#pragma once
+
+#include "gemm.cuh"
+
+namespace sb {
+
+constexpr int kConvWarps = 15;
+constexpr int kConvThreads = kConvWarps * 32;
+constexpr int kConvMmaWarp = 8;
+constexpr int kConvWProducer = 9;
+constexpr int kConvBuilder0 = 10;
+constexpr int kConvWinProducer = 14;
+constexpr int kConvAChunks = 4;  // A chunk buffers in TMEM (32 columns each)
+
+struct ConvTsGeom {
+  int ppt;        // positions per tile
+  int cells;      // output rows per position
+  int xrows;      // X rows per position (window rows = ppt * xrows)
+  int npos;       // positions
+};
+
+__host__ __device__ constexpr int conv_win_box_bytes(int win_rows) { return (win_rows * 128 + 1023) / 1024 * 1024; }
+__host__ __device__ constexpr int conv_ts_smem_bytes(int c, int stages, int win_rows) {
+  return 1024 + stages * c * 128 + 2 * (c / 64) * conv_win_box_bytes(win_rows) + kEpiSmemBytes +
+         8 * (2 * stages + 2 * kConvAChunks + 8) + 16;
+}
+__host__ __device__ constexpr int conv_ts_stages(int c, int win_rows) {
+  int s = kMaxStages;
+  while (s > 2 && conv_ts_smem_bytes(c, s, win_rows) > 227 * 1024) --s;
+  return s;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kConvThreads, 1)
+    conv_ts_kernel(const GemmArgs a, const ConvTsGeom geo, const __grid_constant__ CUtensorMap tmap_x,
+                   const __grid_constant__ CUtensorMap tmap_w, int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int S = stages;
+  const int C = a.n_total;  // == a.bn == a.cin
+  const int nbox = C / 64;
+  const int win_rows = geo.ppt * geo.xrows;
+  const int box_bytes = conv_win_box_bytes(win_rows);
+  const int tile_rows = geo.ppt * geo.cells;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t stage_bytes = C * 128;
+  const uint32_t win_off = S * stage_bytes;                             // [2][nbox][box_bytes]
+  const uint32_t epi_off = win_off + 2 * nbox * box_bytes;
+  float* vecs = reinterpret_cast<float*>(gbase + epi_off);
+  float4* xch_all = reinterpret_cast<float4*>(gbase + epi_off + kEpiVecFloats * 4);
+  const uint32_t bar0 = base + epi_off + kEpiSmemBytes;
+  const uint32_t full_bar = bar0;                         // [S]   weight chunk landed
+  const uint32_t empty_bar = full_bar + 8 * S;            // [S]   weight chunk consumed
+  const uint32_t achf_bar = empty_bar + 8 * S;            // [NA]  A chunk stored in TMEM
+  const uint32_t ache_bar = achf_bar + 8 * kConvAChunks;  // [NA]  A chunk consumed
+  const uint32_t winf_bar = ache_bar + 8 * kConvAChunks;  // [2]   window landed
+  const uint32_t wine_bar = winf_bar + 16;                // [2]   window consumed
+  const uint32_t accf_bar = wine_bar + 16;                // [2]
+  const uint32_t acce_bar = accf_bar + 16;                // [2]
+  const uint32_t tmem_slot = acce_bar + 16;
+  volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
+
+  const int acc_cols = (C + 31) & ~31;
+  const uint32_t a_col0 = 2 * acc_cols;  // A chunk buffers follow the two accumulators
+  const uint32_t ncols = 512;
+
+  const int tiles = (geo.npos + geo.ppt - 1) / geo.ppt;
+  const int nk = a.kpad / kChunkK;  // 7 * C / 64
+
+  if (warp == kConvMmaWarp) {
+    tmem_alloc(tmem_slot, ncols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar + 8 * s, 1);
+      mbar_init(empty_bar + 8 * s, 1);
+    }
+    for (int i = 0; i < kConvAChunks; ++i) {
+      mbar_init(achf_bar + 8 * i, 4);
+      mbar_init(ache_bar + 8 * i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(winf_bar + 8 * i, 1);
+      mbar_init(wine_bar + 8 * i, 4);
+      mbar_init(accf_bar + 8 * i, 1);
+      mbar_init(acce_bar + 8 * i, kEpiWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_w);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+  bool ok = true;
+
+  if (warp == kConvWinProducer) {
+    // ------------------------------------------------------------ window producer
+    if (lane == 0) {
+      int j = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+        const int wb = j & 1;
+        if (ok && !mbar_wait_sleep(wine_bar + 8 * wb, ((j >> 1) & 1) ^ 1)) {
+          ok = false;
+          if (a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
+        }
+        if (!ok) break;
+        mbar_arrive_expect_tx(winf_bar + 8 * wb, nbox * win_rows * 128);
+        const int row0 = t * geo.ppt * geo.xrows;
+        for (int bx = 0; bx < nbox; ++bx)
+          tma_load_2d(base + win_off + (wb * nbox + bx) * box_bytes, &tmap_x, bx * 64, row0, winf_bar + 8 * wb);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kConvWProducer) {
+    // ------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        for (int c = 0; c < nk; ++c, ++it) {
+          const int s = it % S;
+          if (ok && !mbar_wait_sleep(empty_bar + 8 * s, ((it / S) & 1) ^ 1)) {
+            ok = false;
+            if (a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
+          }
+          if (!ok) break;
+          mbar_arrive_expect_tx(full_bar + 8 * s, stage_bytes);
+          tma_load_2d(base + s * stage_bytes, &tmap_w, c * kChunkK, 0, full_bar + 8 * s);
+        }
+        if (!ok) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp >= kConvBuilder0 && warp < kConvBuilder0 + 4) {
+    // ------------------------------------------------------------ A builders
+    const int quad = warp & 3;        // TMEM lanes [32 quad, 32 quad + 32)
+    const int row = quad * 32 + lane; // row within the tile
+    const uint32_t tlane = tmem_base + ((uint32_t)(quad * 32) << 16);
+    uint32_t ac = 0;                  // A chunks produced
+    int j = 0;
+    // this thread's 7 tap rows for tile t (window-local, -1 = zero)
+    auto load_src = [&](int t, int (&src)[7]) {
+      const int m = t * tile_rows + row;
+      const bool live = row < tile_rows && m < a.M && t < tiles;
+      const int w0 = t * geo.ppt * geo.xrows;
+#pragma unroll
+      for (int k = 0; k < 7; ++k) {
+        int v = live ? __ldg(a.gidx + (long long)m * 7 + k) : -1;
+        v = v >= 0 ? v - w0 : -1;
+        src[k] = (v >= 0 && v < win_rows) ? v : -1;
+      }
+    };
+    int src[7], nxt[7];
+    load_src(blockIdx.x, nxt);
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+#pragma unroll
+      for (int k = 0; k < 7; ++k) src[k] = nxt[k];
+      load_src(t + gridDim.x, nxt);  // prefetch the next tile's rows
+      const int wb = j & 1;
+      const bool got = ok && mbar_wait_sleep(winf_bar + 8 * wb, (j >> 1) & 1);
+      ok = __all_sync(0xffffffffu, got) != 0;
+      if (!ok) {
+        if (lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
+        break;
+      }
+      const uint8_t* win = gbase + win_off + wb * nbox * box_bytes;
+      for (int c = 0; c < nk; ++c, ++ac) {
+        const int slot = ac % kConvAChunks;
+        const bool free_ok = mbar_wait_sleep(ache_bar + 8 * slot, ((ac / kConvAChunks) & 1) ^ 1);
+        ok = __all_sync(0xffffffffu, free_ok) != 0;
+        if (!ok) {
+          if (lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
+          break;
+        }
+        tc_fence_after();
+        const int k0 = c * kChunkK;
+        const int tap = k0 / C;
+        const int bx = (k0 - tap * C) >> 6;
+        const int r = src[tap];
+        const uint8_t* rowp = win + bx * box_bytes + (r < 0 ? 0 : r) * 128;
+        uint32_t v[32];
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          uint4 u = make_uint4(0u, 0u, 0u, 0u);
+          if (r >= 0) u = *reinterpret_cast<const uint4*>(rowp + ((p ^ (r & 7)) << 4));
+          v[4 * p] = u.x;
+          v[4 * p + 1] = u.y;
+          v[4 * p + 2] = u.z;
+          v[4 * p + 3] = u.w;
+        }
+        __syncwarp();
+        tmem_st32(tlane + a_col0 + slot * 32, v);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(achf_bar + 8 * slot);
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(wine_bar + 8 * wb);  // window of this tile no longer read
+    }
+  } else if (warp == kConvMmaWarp) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      const uint32_t idesc = mma_idesc(C, std::is_same<T, __nv_bfloat16>::value);
+      const uint64_t bdesc0 = sw128_desc(base);
+      const uint64_t stage_step = stage_bytes >> 4;
+      uint32_t it = 0, ac = 0;
+      int j = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+        const int ab = j & 1;
+        if (ok && !mbar_wait(acce_bar + 8 * ab, ((j >> 1) & 1) ^ 1)) {
+          ok = false;
+          if (a.err) atomicOr(a.err, SB_ERRBIT_MMA_ACC);
+        }
+        tc_fence_after();
+        const uint32_t dacc = tmem_base + ab * acc_cols;
+        for (int c = 0; c < nk; ++c, ++it, ++ac) {
+          const int s = it % S;
+          const int slot = ac % kConvAChunks;
+          if (ok && !mbar_wait(achf_bar + 8 * slot, (ac / kConvAChunks) & 1)) {
+            ok = false;
+            if (a.err) atomicOr(a.err, SB_ERRBIT_MMA_FULL);
+          }
+          if (ok && !mbar_wait(full_bar + 8 * s, (it / S) & 1)) {
+            ok = false;
+            if (a.err) atomicOr(a.err, SB_ERRBIT_MMA_FULL);
+          }
+          tc_fence_after();
+          const uint64_t bd = bdesc0 + s * stage_step;
+          const uint32_t at = tmem_base + a_col0 + slot * 32;
+          if (ok) {
+            tc_mma_f16_ts(dacc, at, bd, idesc, c > 0 ? 1u : 0u);
+            tc_mma_f16_ts_acc(dacc, at + 8, bd + 2, idesc);
+            tc_mma_f16_ts_acc(dacc, at + 16, bd + 4, idesc);
+            tc_mma_f16_ts_acc(dacc, at + 24, bd + 6, idesc);
+          }
+          tc_commit(empty_bar + 8 * s);
+          tc_commit(ache_bar + 8 * slot);
+        }
+        tc_commit(accf_bar + 8 * ab);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int half = warp >> 2;
+    const int bar_id = 3 + quad;
+    float4* xch = xch_all + quad * 64;
+    {
+      float* lnaw = vecs + 1024;
+      for (int i = tid; i < C; i += kEpiWarps * 32) {
+        vecs[i] = __ldg(a.bias + i);
+        lnaw[i] = a.ln_a_w ? __ldg(a.ln_a_w + i) : 0.f;
+        lnaw[256 + i] = a.ln_a_b ? __ldg(a.ln_a_b + i) : 0.f;
+        lnaw[512 + i] = a.ln_b_w ? __ldg(a.ln_b_w + i) : 0.f;
+        lnaw[768 + i] = a.ln_b_b ? __ldg(a.ln_b_b + i) : 0.f;
+        lnaw[1024 + i] = a.gamma ? __ldg(a.gamma + i) : 0.f;
+        lnaw[1280 + i] = a.head_w ? __ldg(a.head_w + i) : 0.f;
+      }
+      asm volatile("bar.sync 2, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
+    }
+    const EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768,
+                     vecs + 1024 + 1024, vecs + 1024 + 1280};
+    int j = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+      const int ab = j & 1;
+      const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (j >> 1) & 1);
+      ok = __all_sync(0xffffffffu, got) != 0;
+      ok = bar_red_and(bar_id, 64, ok);
+      if (!ok && lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_EPILOGUE);
+      tc_fence_after();
+      if (ok) {
+        const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
+        epilogue_tile<T>(a, ev, xch, bar_id, half, t * tile_rows + quad * 32, quad * 32, tile_rows, 0, trow, lane);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar + 8 * ab);
+    }
+  }
+
+  if (!ok && a.err) atomicOr(a.err, 1);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kConvMmaWarp) tmem_dealloc(tmem_base, ncols);
+}
+
+}  // namespace sb

@@ -421,13 +421,17 @@ __device__ __forceinline__ void epi_chunk_lnb(const GemmArgs& a, const EpiVecs& 
 }
 
 template <typename T>
+// m_first: GEMM row of this thread's lane 0; tile_row: its row within the
+// tile; rows at or past `tile_rows` within the tile (padding of position-
+// aligned tiles) or past M are never stored.
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& ev, float4* xch, int bar_id,
-                                              int half, int m_first, int n0, uint32_t tbase, int lane) {
+                                              int half, int m_first, int tile_row, int tile_rows, int n0,
+                                              uint32_t tbase, int lane) {
   // No branch below depends on the lane: rows past M are clamped onto row
   // M-1 for every load and only the stores are predicated.
   EpiRow r;
   const int m = m_first + lane;
-  r.valid = m < a.M;
+  r.valid = m < a.M && tile_row + lane < tile_rows;
   r.mc = r.valid ? m : a.M - 1;
   r.orow = (a.gidx && a.orow_from_gidx) ? (long long)__ldg(a.gidx + (long long)r.mc * a.taps) : (long long)r.mc;
   const int fl = a.flags;
@@ -764,7 +768,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
-        epilogue_tile<T>(a, ev, xch, bar_id, half, mt * kBlockM + quad * 32, nt * a.bn, trow, lane);
+        epilogue_tile<T>(a, ev, xch, bar_id, half, mt * kBlockM + quad * 32, quad * 32, kBlockM, nt * a.bn, trow,
+                         lane);
       }
       tc_fence_before();
       __syncwarp();
