@@ -13,6 +13,10 @@ from .build import lib_path
 
 MAX_BLOCKS = 32
 SB_OK = 0
+SB_ERR_INVALID_ARG = 1
+SB_ERR_UNSUPPORTED = 2
+SB_ERR_CUDA = 3
+SB_ERR_WORKSPACE = 4
 
 DT_F32, DT_F16, DT_BF16, DT_I64, DT_I32, DT_U8, DT_I16, DT_U16 = range(8)
 
@@ -24,6 +28,7 @@ EXPORTED = (
     "sb_build_gather_index",
     "sb_build_pair_u8",
     "sb_hex_conv",
+    "sb_hex_conv_noalloc",
     "sb_hex_conv_ln",
     "sb_hex_conv_workspace_bytes",
     "sb_attn_pair",
@@ -108,6 +113,7 @@ def lib() -> C.CDLL:
         "sb_build_gather_index": ([_P, i32, i32, i32, _P, _P, _P], i32),
         "sb_build_pair_u8": ([_P, i32, _P, i32, i32, i32, _P, _P, _P], i32),
         "sb_hex_conv": ([_P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P, sz, _P], i32),
+        "sb_hex_conv_noalloc": ([_P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P], i32),
         "sb_hex_conv_ln": ([_P, _P, _P, _P, _P, _P, _P, f32, i32, i32, i32, i32, i32, _P, _P, sz, _P], i32),
         "sb_hex_conv_workspace_bytes": ([i32, i32, C.POINTER(sz)], i32),
         "sb_attn_pair": ([_P, _P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P], i32),

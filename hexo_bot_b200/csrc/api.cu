@@ -603,6 +603,41 @@ int sb_hex_conv(const void* x, const int32_t* gather_idx, const uint8_t* mask, c
                          workspace, workspace_bytes, stream);
 }
 
+// ---- allocation-free hex_conv --------------------------------------------------
+// Scratch of sb_hex_conv_noalloc: a fixed file-scope device array (absolute
+// gather table + row mask), so the call needs no caller workspace and the
+// library still allocates nothing at run time.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB: up to 262,141 rows (batch * npad)
+constexpr long long kNoAllocMaxRows = 262141;       // largest batch * npad whose workspace fits
+static __device__ __align__(256) uint8_t g_hex_conv_scratch[kNoAllocScratchBytes];
+
+int sb_hex_conv_noalloc(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w,
+                        const float* bias, int batch, int npad, int cin, int cout, void* out, void* stream) {
+  if (batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "hex_conv_noalloc: bad args");
+  size_t need = 0;
+  sb_hex_conv_workspace_bytes(batch, npad, &need);
+  if (need > kNoAllocScratchBytes)
+    return fail(SB_ERR_UNSUPPORTED,
+                "hex_conv_noalloc: batch*npad=%lld rows need %zu scratch bytes; the fixed scratch holds %zu "
+                "(at most %lld rows)",
+                (long long)batch * npad, need, kNoAllocScratchBytes, kNoAllocMaxRows);
+  // Per-device symbol address, resolved on the first call on each device
+  // (that call does the set-up; later calls only read the cache).
+  static void* scratch[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(SB_ERR_CUDA, "hex_conv_noalloc: no current device");
+  if (!scratch[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_hex_conv_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(SB_ERR_CUDA, "hex_conv_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    scratch[dev] = ptr;
+  }
+  return hex_conv_common(x, gather_idx, mask, w, bias, nullptr, nullptr, 0.f, 0, batch, npad, cin, cout, out,
+                         scratch[dev], kNoAllocScratchBytes, stream);
+}
+
 int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w, const float* bias,
                    const float* ln_w, const float* ln_b, float eps, int relu, int batch, int npad, int cin, int cout,
                    void* out, void* workspace, size_t workspace_bytes, void* stream) {

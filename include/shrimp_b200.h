@@ -158,6 +158,20 @@ int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask
                    const float* bias, const float* ln_w, const float* ln_b, float eps, int relu, int batch,
                    int npad, int cin, int cout, void* out, void* workspace, size_t workspace_bytes,
                    void* stream);
+/* sb_hex_conv without a caller workspace (no counterpart in the reference).
+ * For callers that cannot hand the library device memory at call time -
+ * e.g. code that must not allocate between steps of a serving loop, or a
+ * host that owns no allocator for scratch - the scratch lives in a fixed
+ * 8 MiB device array inside the library: batch * npad must be <= 262,141
+ * rows, larger calls fail with SB_ERR_UNSUPPORTED. The library allocates
+ * nothing (no cudaMalloc / cudaFree). The first call on each device resolves
+ * the array's address (set-up; make it before any stream capture); nothing in
+ * the scratch needs to start at zero (each call writes what it reads). Calls
+ * share the one array per device, so calls that overlap in time on the same
+ * device (different streams or threads) race: serialise them. Same results
+ * as sb_hex_conv. */
+int sb_hex_conv_noalloc(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w_packed,
+                        const float* bias, int batch, int npad, int cin, int cout, void* out, void* stream);
 /* Workspace for sb_hex_conv / sb_hex_conv_ln. */
 int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes);
 /* shrimp::attn_pair (_triton_attn.py:132-171): q, k, v (B, H, S, D) f16 with
