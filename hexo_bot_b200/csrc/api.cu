@@ -181,13 +181,15 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
 }
 
 // Position-windowed 7-tap conv (conv_ts_kernel) when the shape allows it:
-// C = Cin = Cout a multiple of 64 up to 256, whole positions of <= 128 cells
+// C = Cin = Cout in {64, 128, 192}, whole positions of <= 128 cells
 // per 128-row tile, a window of <= 256 X rows. Returns 1 when not eligible
 // (the caller then runs the gather-GEMM), else an sb_status.
 template <typename T>
 int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) {
   const int C = a.n_total;
-  if (a.taps != 7 || !a.gidx || a.cin != C || C % 64 || C > 256 || cells <= 0 || cells > kBlockM || xrows < cells)
+  // TMEM: two C-column accumulators plus >= 2 A slots of 32 columns in 512.
+  if (a.taps != 7 || !a.gidx || a.cin != C || C % 64 || 2 * C + 64 > 512 || cells <= 0 || cells > kBlockM ||
+      xrows < cells)
     return 1;
   if (a.lda != C || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16 || producer_mode() == 1) return 1;
   int ppt = kBlockM / cells;

@@ -28,7 +28,8 @@ constexpr int kConvMmaWarp = 8;
 constexpr int kConvWProducer = 9;
 constexpr int kConvBuilder0 = 10;
 constexpr int kConvWinProducer = 14;
-constexpr int kConvAChunks = 4;  // A chunk buffers in TMEM (32 columns each)
+constexpr int kConvMaxStages = 8;
+constexpr int kConvStageChunks = 2;  // 64-wide K chunks per ring stage (one barrier round trip per 8 MMAs)
 
 struct ConvTsGeom {
   int ppt;        // positions per tile
@@ -39,12 +40,16 @@ struct ConvTsGeom {
 
 __host__ __device__ constexpr int conv_win_box_bytes(int win_rows) { return (win_rows * 128 + 1023) / 1024 * 1024; }
 __host__ __device__ constexpr int conv_ts_smem_bytes(int c, int stages, int win_rows) {
-  return 1024 + stages * c * 128 + 2 * (c / 64) * conv_win_box_bytes(win_rows) + kEpiSmemBytes +
-         8 * (2 * stages + 2 * kConvAChunks + 8) + 16;
+  return 1024 + stages * kConvStageChunks * c * 128 + 2 * (c / 64) * conv_win_box_bytes(win_rows) + kEpiSmemBytes +
+         8 * (2 * stages + 8) + 16;
 }
+// Ring depth: limited by shared memory and by TMEM (two C-column accumulators
+// plus 32 columns per A chunk of each stage, within 512 columns).
 __host__ __device__ constexpr int conv_ts_stages(int c, int win_rows) {
-  int s = kMaxStages;
-  while (s > 2 && conv_ts_smem_bytes(c, s, win_rows) > 227 * 1024) --s;
+  int s = kConvMaxStages;
+  while (s > 2 && (conv_ts_smem_bytes(c, s, win_rows) > 227 * 1024 ||
+                   2 * ((c + 31) / 32 * 32) + 32 * kConvStageChunks * s > 512))
+    --s;
   return s;
 }
 
@@ -66,17 +71,19 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t stage_bytes = C * 128;
+  const uint32_t chunk_bytes = C * 128;                 // one 64-wide K chunk of the weights
+  const uint32_t stage_bytes = kConvStageChunks * chunk_bytes;
   const uint32_t win_off = S * stage_bytes;                             // [2][nbox][box_bytes]
   const uint32_t epi_off = win_off + 2 * nbox * box_bytes;
   float* vecs = reinterpret_cast<float*>(gbase + epi_off);
   float4* xch_all = reinterpret_cast<float4*>(gbase + epi_off + kEpiVecFloats * 4);
   const uint32_t bar0 = base + epi_off + kEpiSmemBytes;
-  const uint32_t full_bar = bar0;                         // [S]   weight chunk landed
-  const uint32_t empty_bar = full_bar + 8 * S;            // [S]   weight chunk consumed
-  const uint32_t achf_bar = empty_bar + 8 * S;            // [NA]  A chunk stored in TMEM
-  const uint32_t ache_bar = achf_bar + 8 * kConvAChunks;  // [NA]  A chunk consumed
-  const uint32_t winf_bar = ache_bar + 8 * kConvAChunks;  // [2]   window landed
+  // Stage s = weight chunk in shared memory + A chunk in TMEM slot s: full
+  // when the TMA bytes landed and the four A builders stored their rows;
+  // empty when the MMAs that read both completed.
+  const uint32_t full_bar = bar0;                         // [S]
+  const uint32_t empty_bar = full_bar + 8 * S;            // [S]
+  const uint32_t winf_bar = empty_bar + 8 * S;            // [2]   window landed
   const uint32_t wine_bar = winf_bar + 16;                // [2]   window consumed
   const uint32_t accf_bar = wine_bar + 16;                // [2]
   const uint32_t acce_bar = accf_bar + 16;                // [2]
@@ -88,7 +95,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const uint32_t ncols = 512;
 
   const int tiles = (geo.npos + geo.ppt - 1) / geo.ppt;
-  const int nk = a.kpad / kChunkK;  // 7 * C / 64
+  const int nk = a.kpad / kChunkK;  // 7 * C / 64 chunks per tile
+  const int nst = (nk + kConvStageChunks - 1) / kConvStageChunks;  // ring stages per tile
 
   if (warp == kConvMmaWarp) {
     tmem_alloc(tmem_slot, ncols);
@@ -96,12 +104,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar + 8 * s, 1);
+      mbar_init(full_bar + 8 * s, 1 + 4);
       mbar_init(empty_bar + 8 * s, 1);
-    }
-    for (int i = 0; i < kConvAChunks; ++i) {
-      mbar_init(achf_bar + 8 * i, 4);
-      mbar_init(ache_bar + 8 * i, 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(winf_bar + 8 * i, 1);
@@ -142,15 +146,18 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-        for (int c = 0; c < nk; ++c, ++it) {
+        for (int q = 0; q < nst; ++q, ++it) {
           const int s = it % S;
+          const int nc = min(kConvStageChunks, nk - q * kConvStageChunks);
           if (ok && !mbar_wait_sleep(empty_bar + 8 * s, ((it / S) & 1) ^ 1)) {
             ok = false;
             if (a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
           }
           if (!ok) break;
-          mbar_arrive_expect_tx(full_bar + 8 * s, stage_bytes);
-          tma_load_2d(base + s * stage_bytes, &tmap_w, c * kChunkK, 0, full_bar + 8 * s);
+          mbar_arrive_expect_tx(full_bar + 8 * s, nc * chunk_bytes);
+          for (int h = 0; h < nc; ++h)
+            tma_load_2d(base + s * stage_bytes + h * chunk_bytes, &tmap_w, (q * kConvStageChunks + h) * kChunkK, 0,
+                        full_bar + 8 * s);
         }
         if (!ok) break;
       }
@@ -189,37 +196,57 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         break;
       }
       const uint8_t* win = gbase + win_off + wb * nbox * box_bytes;
-      for (int c = 0; c < nk; ++c, ++ac) {
-        const int slot = ac % kConvAChunks;
-        const bool free_ok = mbar_wait_sleep(ache_bar + 8 * slot, ((ac / kConvAChunks) & 1) ^ 1);
+      // gather chunk c of this thread's row from the window (zeros for a
+      // missing tap) into 32 registers
+      auto gather = [&](int c, uint32_t (&v)[32]) {
+        const int k0 = c * kChunkK;
+        const int tap = k0 / C;
+        const int bx = (k0 - tap * C) >> 6;
+        int r = src[0];
+#pragma unroll
+        for (int k = 1; k < 7; ++k) r = tap == k ? src[k] : r;  // registers, no local array
+        // branch-free: a missing tap reads row 0 and is masked to zero
+        const int rr = r < 0 ? 0 : r;
+        const uint32_t keep = r < 0 ? 0u : 0xffffffffu;
+        const uint8_t* rowp = win + bx * box_bytes + rr * 128;
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((p ^ (rr & 7)) << 4));
+          v[4 * p] = u.x & keep;
+          v[4 * p + 1] = u.y & keep;
+          v[4 * p + 2] = u.z & keep;
+          v[4 * p + 3] = u.w & keep;
+        }
+      };
+      // Software pipeline: the gather of chunk c + 1 overlaps the TMEM store
+      // of chunk c; a stage (two chunks) is published once its stores have
+      // completed.
+      uint32_t va[32], vb[32];
+      gather(0, va);
+      for (int q = 0; q < nst; ++q) {
+        const uint32_t ai = ac + q;
+        const int slot = ai % S;
+        const bool free_ok = mbar_wait(empty_bar + 8 * slot, ((ai / S) & 1) ^ 1);
         ok = __all_sync(0xffffffffu, free_ok) != 0;
         if (!ok) {
           if (lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
           break;
         }
         tc_fence_after();
-        const int k0 = c * kChunkK;
-        const int tap = k0 / C;
-        const int bx = (k0 - tap * C) >> 6;
-        const int r = src[tap];
-        const uint8_t* rowp = win + bx * box_bytes + (r < 0 ? 0 : r) * 128;
-        uint32_t v[32];
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          uint4 u = make_uint4(0u, 0u, 0u, 0u);
-          if (r >= 0) u = *reinterpret_cast<const uint4*>(rowp + ((p ^ (r & 7)) << 4));
-          v[4 * p] = u.x;
-          v[4 * p + 1] = u.y;
-          v[4 * p + 2] = u.z;
-          v[4 * p + 3] = u.w;
-        }
+        const int c0 = q * kConvStageChunks;
         __syncwarp();
-        tmem_st32(tlane + a_col0 + slot * 32, v);
+        tmem_st32(tlane + a_col0 + slot * (32 * kConvStageChunks), va);
+        if (c0 + 1 < nk) gather(c0 + 1, vb);
+        __syncwarp();
+        if (c0 + 1 < nk) tmem_st32(tlane + a_col0 + slot * (32 * kConvStageChunks) + 32, vb);
+        if (c0 + 2 < nk) gather(c0 + 2, va);
+        __syncwarp();
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(achf_bar + 8 * slot);
+        if (lane == 0) mbar_arrive(full_bar + 8 * slot);
       }
+      ac += nst;
       if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(wine_bar + 8 * wb);  // window of this tile no longer read
@@ -230,7 +257,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const uint32_t idesc = mma_idesc(C, std::is_same<T, __nv_bfloat16>::value);
       const uint64_t bdesc0 = sw128_desc(base);
       const uint64_t stage_step = stage_bytes >> 4;
-      uint32_t it = 0, ac = 0;
+      const uint64_t chunk_step = chunk_bytes >> 4;
+      uint32_t it = 0;
       int j = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
         const int ab = j & 1;
@@ -240,28 +268,25 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         }
         tc_fence_after();
         const uint32_t dacc = tmem_base + ab * acc_cols;
-        for (int c = 0; c < nk; ++c, ++it, ++ac) {
+        for (int q = 0; q < nst; ++q, ++it) {
           const int s = it % S;
-          const int slot = ac % kConvAChunks;
-          if (ok && !mbar_wait(achf_bar + 8 * slot, (ac / kConvAChunks) & 1)) {
-            ok = false;
-            if (a.err) atomicOr(a.err, SB_ERRBIT_MMA_FULL);
-          }
+          const int nc = min(kConvStageChunks, nk - q * kConvStageChunks);
           if (ok && !mbar_wait(full_bar + 8 * s, (it / S) & 1)) {
             ok = false;
             if (a.err) atomicOr(a.err, SB_ERRBIT_MMA_FULL);
           }
           tc_fence_after();
-          const uint64_t bd = bdesc0 + s * stage_step;
-          const uint32_t at = tmem_base + a_col0 + slot * 32;
           if (ok) {
-            tc_mma_f16_ts(dacc, at, bd, idesc, c > 0 ? 1u : 0u);
-            tc_mma_f16_ts_acc(dacc, at + 8, bd + 2, idesc);
-            tc_mma_f16_ts_acc(dacc, at + 16, bd + 4, idesc);
-            tc_mma_f16_ts_acc(dacc, at + 24, bd + 6, idesc);
+            for (int h = 0; h < nc; ++h) {
+              const uint64_t bd = bdesc0 + s * stage_step + h * chunk_step;
+              const uint32_t at = tmem_base + a_col0 + s * (32 * kConvStageChunks) + h * 32;
+              tc_mma_f16_ts(dacc, at, bd, idesc, (q > 0 || h > 0) ? 1u : 0u);
+              tc_mma_f16_ts_acc(dacc, at + 8, bd + 2, idesc);
+              tc_mma_f16_ts_acc(dacc, at + 16, bd + 4, idesc);
+              tc_mma_f16_ts_acc(dacc, at + 24, bd + 6, idesc);
+            }
           }
           tc_commit(empty_bar + 8 * s);
-          tc_commit(ache_bar + 8 * slot);
         }
         tc_commit(accf_bar + 8 * ab);
       }
@@ -289,8 +314,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768,
                      vecs + 1024 + 1024, vecs + 1024 + 1280};
     int j = 0;
+    EpiRow row = make_epi_row(a, blockIdx.x * tile_rows + quad * 32, quad * 32, tile_rows, lane);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
       const int ab = j & 1;
+      const int tn = t + gridDim.x;  // next tile's rows: loads in flight during this tile
+      const EpiRow row_next = make_epi_row(a, tn * tile_rows + quad * 32, quad * 32, tile_rows, lane);
       const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (j >> 1) & 1);
       ok = __all_sync(0xffffffffu, got) != 0;
       ok = bar_red_and(bar_id, 64, ok);
@@ -298,11 +326,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       tc_fence_after();
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
-        epilogue_tile<T>(a, ev, xch, bar_id, half, t * tile_rows + quad * 32, quad * 32, tile_rows, 0, trow, lane);
+        epilogue_tile<T>(a, ev, xch, bar_id, half, row, 0, trow, lane);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar + 8 * ab);
+      row = row_next;
     }
   }
 

@@ -346,6 +346,43 @@ struct EpiRow {
   bool lnb_row;     // LayerNorm B applies to this row
 };
 
+// Row context of this thread for a tile (m_first: GEMM row of lane 0;
+// tile_row: its row within the tile; rows at or past `tile_rows` within the
+// tile, the padding of position-aligned tiles, or past M are never stored).
+// Callers build it one tile ahead so the loads overlap the current tile.
+__device__ __forceinline__ EpiRow make_epi_row(const GemmArgs& a, int m_first, int tile_row, int tile_rows,
+                                               int lane) {
+  // No branch depends on the lane: rows past M are clamped onto row M-1.
+  EpiRow r;
+  const int m = m_first + lane;
+  r.valid = m < a.M && tile_row + lane < tile_rows;
+  r.mc = r.valid ? m : a.M - 1;
+  r.orow = (a.gidx && a.orow_from_gidx) ? (long long)__ldg(a.gidx + (long long)r.mc * a.taps) : (long long)r.mc;
+  const int fl = a.flags;
+  r.mk = ((fl & (EPI_MASK | EPI_HEAD)) && a.rowmask) ? __ldg(a.rowmask + r.orow) : 1.f;
+  r.lnb_row = (fl & EPI_LN_B) != 0;
+  if (fl & EPI_LNB_TOKENS) r.lnb_row = r.lnb_row && r.valid && (r.orow % a.seq_len) < a.ntok;
+  return r;
+}
+
+// registers -> TMEM for W (16 or 32) columns of this thread's row
+template <int W>
+__device__ __forceinline__ void tmem_stw(uint32_t taddr, const float (&v)[32]) {
+  uint32_t u[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(v[i]);
+  if (W == 32) {
+    tmem_st32(taddr, u);
+  } else {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr),
+        "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]), "r"(u[8]),
+        "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15])
+        : "memory");
+  }
+}
+
 // Main pass over one chunk of W columns [c, c + W) of the tile (tile-local
 // column c, global column n0 + c).
 template <typename T, int W>
@@ -353,7 +390,10 @@ __device__ __forceinline__ void epi_chunk_main(const GemmArgs& a, const EpiVecs&
                                                uint32_t tcol, float mean_a, float rstd_a, float& head,
                                                float& cntb, float& meanb, float& m2b) {
   const int fl = a.flags;
-  float v[32], t[32];
+  float v[32], t[32], x[32];
+  // global loads first: their latency overlaps the TMEM read and the math
+  if (fl & EPI_RESID) ld_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, x, r.valid);
+  if (fl & EPI_RES16) ld_row16<T, W>(reinterpret_cast<const T*>(a.res16) + r.orow * a.ldr16 + n0 + c, x, true);
   tmem_ldw<W>(tcol, v);
   ld_vec<W>(ev.bias + n0 + c, t);
 #pragma unroll
@@ -384,8 +424,6 @@ __device__ __forceinline__ void epi_chunk_main(const GemmArgs& a, const EpiVecs&
     for (int i = 0; i < W; ++i) v[i] *= r.mk;
   }
   if (fl & EPI_RESID) {
-    float x[32];
-    ld_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, x, r.valid);
     ld_vec<W>(ev.gamma + c, t);
 #pragma unroll
     for (int i = 0; i < W; ++i) v[i] = fmaf(v[i], t[i], x[i]);
@@ -395,22 +433,24 @@ __device__ __forceinline__ void epi_chunk_main(const GemmArgs& a, const EpiVecs&
     for (int i = 0; i < W; ++i) v[i] = fmaxf(v[i], 0.f);
   }
   if (fl & EPI_RES16) {
-    ld_row16<T, W>(reinterpret_cast<const T*>(a.res16) + r.orow * a.ldr16 + n0 + c, t, true);
 #pragma unroll
-    for (int i = 0; i < W; ++i) v[i] = fmaxf(v[i] + t[i], 0.f);
+    for (int i = 0; i < W; ++i) v[i] = fmaxf(v[i] + x[i], 0.f);
   }
-  if (fl & EPI_LN_B) stats_merge_w<W>(cntb, meanb, m2b, v);
+  if (fl & EPI_LN_B) {
+    stats_merge_w<W>(cntb, meanb, m2b, v);
+    tmem_stw<W>(tcol, v);  // the accumulator columns hold v for the LayerNorm B pass
+  }
   if (fl & (EPI_RESID | EPI_OUT32)) st_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, v, r.valid);
   if (fl & EPI_OUT16) st_row16<T, W>(reinterpret_cast<T*>(a.out16) + r.orow * a.ld16 + n0 + c, v,
                                      r.valid && !r.lnb_row);
 }
 
-// LayerNorm B over the stored fp32 row (re-read: this thread wrote it).
+// LayerNorm B over the row values the main pass parked in TMEM.
 template <typename T, int W>
 __device__ __forceinline__ void epi_chunk_lnb(const GemmArgs& a, const EpiVecs& ev, const EpiRow& r, int n0, int c,
-                                              float meanb, float rstd_b) {
+                                              uint32_t tcol, float meanb, float rstd_b) {
   float v[32], w[32], t[32];
-  ld_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, v, r.valid);
+  tmem_ldw<W>(tcol, v);
   ld_vec<W>(ev.lnbw + c, w);
   ld_vec<W>(ev.lnbb + c, t);
 #pragma unroll
@@ -421,24 +461,9 @@ __device__ __forceinline__ void epi_chunk_lnb(const GemmArgs& a, const EpiVecs& 
 }
 
 template <typename T>
-// m_first: GEMM row of this thread's lane 0; tile_row: its row within the
-// tile; rows at or past `tile_rows` within the tile (padding of position-
-// aligned tiles) or past M are never stored.
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& ev, float4* xch, int bar_id,
-                                              int half, int m_first, int tile_row, int tile_rows, int n0,
-                                              uint32_t tbase, int lane) {
-  // No branch below depends on the lane: rows past M are clamped onto row
-  // M-1 for every load and only the stores are predicated.
-  EpiRow r;
-  const int m = m_first + lane;
-  r.valid = m < a.M && tile_row + lane < tile_rows;
-  r.mc = r.valid ? m : a.M - 1;
-  r.orow = (a.gidx && a.orow_from_gidx) ? (long long)__ldg(a.gidx + (long long)r.mc * a.taps) : (long long)r.mc;
+                                              int half, const EpiRow& r, int n0, uint32_t tbase, int lane) {
   const int fl = a.flags;
-  r.mk = ((fl & (EPI_MASK | EPI_HEAD)) && a.rowmask) ? __ldg(a.rowmask + r.orow) : 1.f;
-  r.lnb_row = (fl & EPI_LN_B) != 0;
-  if (fl & EPI_LNB_TOKENS) r.lnb_row = r.lnb_row && r.valid && (r.orow % a.seq_len) < a.ntok;
-
   const int hw = a.bn >> 1;                     // columns per half
   const int c_lo = half * hw, c_hi = c_lo + hw;  // tile-local columns of this warp
   float4* xme = xch + half * 32 + lane;
@@ -488,10 +513,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& 
   if (fl & EPI_LN_B) {
     stats_combine(cntb, meanb, m2b, xme, xot, bar_id, half);
     const float rstd_b = rsqrtf(m2b / fmaxf(cntb, 1.f) + a.eps);
-    // the fp32 row pieces this thread stored above must be visible to its own re-read
+    tmem_wait_st();  // the parked values are in TMEM before they are read back
     int c = c_lo;
-    for (; c + 32 <= c_hi; c += 32) epi_chunk_lnb<T, 32>(a, ev, r, n0, c, meanb, rstd_b);
-    if (c < c_hi) epi_chunk_lnb<T, 16>(a, ev, r, n0, c, meanb, rstd_b);
+    for (; c + 32 <= c_hi; c += 32) epi_chunk_lnb<T, 32>(a, ev, r, n0, c, tbase + c, meanb, rstd_b);
+    if (c < c_hi) epi_chunk_lnb<T, 16>(a, ev, r, n0, c, tbase + c, meanb, rstd_b);
   }
 }
 
@@ -754,9 +779,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768,
                      vecs + 1024 + 1024, vecs + 1024 + 1280};
     int j = 0;
+    EpiRow row = make_epi_row(a, (blockIdx.x / n_tiles) * kBlockM + quad * 32, quad * 32, kBlockM, lane);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
-      const int nt = t % n_tiles, mt = t / n_tiles;
+      const int nt = t % n_tiles;
       const int ab = j & 1;
+      const int tn = t + gridDim.x;  // next tile's rows: loads in flight during this tile
+      const EpiRow row_next = make_epi_row(a, (tn / n_tiles) * kBlockM + quad * 32, quad * 32, kBlockM, lane);
       // every lane waits (no lane-dependent control flow ahead of the
       // .sync.aligned TMEM loads of the epilogue)
       const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (j >> 1) & 1);
@@ -768,12 +796,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
-        epilogue_tile<T>(a, ev, xch, bar_id, half, mt * kBlockM + quad * 32, quad * 32, kBlockM, nt * a.bn, trow,
-                         lane);
+        epilogue_tile<T>(a, ev, xch, bar_id, half, row, nt * a.bn, trow, lane);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar + 8 * ab);
+      row = row_next;
     }
   }
 
