@@ -170,10 +170,16 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
   }
   const int stages = gemm_stages(a.bn, a.taps);
   const int smem = gemm_smem_bytes(a.bn, stages, a.taps);
-  if (int s = ensure_smem(reinterpret_cast<const void*>(gemm_ws_kernel<T>), smem)) return s;
+  const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B)) != 0;
+  const void* fn = heavy ? reinterpret_cast<const void*>(gemm_ws_kernel<T, true>)
+                         : reinterpret_cast<const void*>(gemm_ws_kernel<T, false>);
+  if (int s = ensure_smem(fn, smem)) return s;
   const long long tiles = cdiv(a.M, kBlockM) * (a.n_total / a.bn);
   const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-  gemm_ws_kernel<T><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, stages);
+  if (heavy)
+    gemm_ws_kernel<T, true><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, stages);
+  else
+    gemm_ws_kernel<T, false><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, stages);
   if (sync_debug())
     fprintf(stderr, "[sb] gemm M=%d N=%d bn=%d kpad=%d taps=%d cin=%d tma=%d stages=%d smem=%d grid=%d flags=%d\n",
             a.M, a.n_total, a.bn, a.kpad, a.taps, a.cin, a.use_tma, stages, smem, grid, a.flags);
@@ -208,11 +214,17 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
   memset(&mw, 0, sizeof(mw));
   if (int s = make_tmap(&mx, a.A, bf16, C, (long long)npos * xrows, C, win_rows)) return s;
   if (int s = make_tmap(&mw, a.Bw, bf16, a.kpad, C, a.kpad, C)) return s;
-  if (int s = ensure_smem(reinterpret_cast<const void*>(conv_ts_kernel<T>), smem)) return s;
+  const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B)) != 0;
+  const void* fn = heavy ? reinterpret_cast<const void*>(conv_ts_kernel<T, true>)
+                         : reinterpret_cast<const void*>(conv_ts_kernel<T, false>);
+  if (int s = ensure_smem(fn, smem)) return s;
   ConvTsGeom geo{ppt, cells, xrows, npos};
   const int tiles = (npos + ppt - 1) / ppt;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  conv_ts_kernel<T><<<grid, kConvThreads, smem, st>>>(a, geo, mx, mw, stages);
+  if (heavy)
+    conv_ts_kernel<T, true><<<grid, kConvThreads, smem, st>>>(a, geo, mx, mw, stages);
+  else
+    conv_ts_kernel<T, false><<<grid, kConvThreads, smem, st>>>(a, geo, mx, mw, stages);
   if (sync_debug())
     fprintf(stderr, "[sb] conv_ts M=%d C=%d ppt=%d win=%d stages=%d smem=%d grid=%d flags=%d\n", a.M, C, ppt,
             win_rows, stages, smem, grid, a.flags);

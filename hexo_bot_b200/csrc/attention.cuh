@@ -199,8 +199,15 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
         }
         __syncthreads();
       }
-      for (int i = tid; i < SP * SP; i += kAttnThreads) {
-        const int qi = i / SP, ki = i - qi * SP;
+      // rows across warps, keys across lanes (no division per entry): lane L
+      // of warp w visits entries L, L + 32, ... of the rows w, w + 8, ...
+      int qi = warp, ki = lane;
+      while (ki >= SP) {
+        ki -= SP;
+        qi += kAttnWarps;
+      }
+      while (qi < SP) {
+        const int i = qi * SP + ki;
         int row = kRowExcluded;
         if (ki < n_keys) {
           if (qi >= S) {
@@ -225,6 +232,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
           }
         }
         rowtab[i] = (uint8_t)row;
+        ki += 32;
+        while (ki >= SP) {
+          ki -= SP;
+          qi += kAttnWarps;
+        }
       }
     }
 

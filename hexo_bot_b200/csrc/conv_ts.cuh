@@ -53,7 +53,7 @@ __host__ __device__ constexpr int conv_ts_stages(int c, int win_rows) {
   return s;
 }
 
-template <typename T>
+template <typename T, bool HEAVY>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv_ts_kernel(const GemmArgs a, const ConvTsGeom geo, const __grid_constant__ CUtensorMap tmap_x,
                    const __grid_constant__ CUtensorMap tmap_w, int stages) {
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       tc_fence_after();
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
-        epilogue_tile<T>(a, ev, xch, bar_id, half, row, 0, trow, lane);
+        epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, 0, trow, lane);
       }
       tc_fence_before();
       __syncwarp();

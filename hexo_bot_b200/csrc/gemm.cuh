@@ -385,15 +385,19 @@ __device__ __forceinline__ void tmem_stw(uint32_t taddr, const float (&v)[32]) {
 
 // Main pass over one chunk of W columns [c, c + W) of the tile (tile-local
 // column c, global column n0 + c).
-template <typename T, int W>
+// HEAVY: compiled with the residual / LayerNorm-B paths (flags EPI_RESID,
+// EPI_RES16, EPI_LN_B); the light instantiation leaves them out so the other
+// epilogues keep their registers.
+template <typename T, int W, bool HEAVY>
 __device__ __forceinline__ void epi_chunk_main(const GemmArgs& a, const EpiVecs& ev, const EpiRow& r, int n0, int c,
                                                uint32_t tcol, float mean_a, float rstd_a, float& head,
                                                float& cntb, float& meanb, float& m2b) {
-  const int fl = a.flags;
+  const int fl = HEAVY ? a.flags : (a.flags & ~(EPI_RESID | EPI_RES16 | EPI_LN_B));
   float v[32], t[32], x[32];
   // global loads first: their latency overlaps the TMEM read and the math
-  if (fl & EPI_RESID) ld_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, x, r.valid);
-  if (fl & EPI_RES16) ld_row16<T, W>(reinterpret_cast<const T*>(a.res16) + r.orow * a.ldr16 + n0 + c, x, true);
+  if (HEAVY && (fl & EPI_RESID)) ld_row32<W>(a.out32 + r.orow * a.ld32 + n0 + c, x, r.valid);
+  if (HEAVY && (fl & EPI_RES16))
+    ld_row16<T, W>(reinterpret_cast<const T*>(a.res16) + r.orow * a.ldr16 + n0 + c, x, true);
   tmem_ldw<W>(tcol, v);
   ld_vec<W>(ev.bias + n0 + c, t);
 #pragma unroll
@@ -460,10 +464,10 @@ __device__ __forceinline__ void epi_chunk_lnb(const GemmArgs& a, const EpiVecs& 
   if (a.flags & EPI_OUT16) st_row16<T, W>(reinterpret_cast<T*>(a.out16) + r.orow * a.ld16 + n0 + c, v, okb);
 }
 
-template <typename T>
+template <typename T, bool HEAVY>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& ev, float4* xch, int bar_id,
                                               int half, const EpiRow& r, int n0, uint32_t tbase, int lane) {
-  const int fl = a.flags;
+  const int fl = HEAVY ? a.flags : (a.flags & ~(EPI_RESID | EPI_RES16 | EPI_LN_B));
   const int hw = a.bn >> 1;                     // columns per half
   const int c_lo = half * hw, c_hi = c_lo + hw;  // tile-local columns of this warp
   float4* xme = xch + half * 32 + lane;
@@ -498,8 +502,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& 
   {
     int c = c_lo;
     for (; c + 32 <= c_hi; c += 32)
-      epi_chunk_main<T, 32>(a, ev, r, n0, c, tbase + c, mean_a, rstd_a, head, cntb, meanb, m2b);
-    if (c < c_hi) epi_chunk_main<T, 16>(a, ev, r, n0, c, tbase + c, mean_a, rstd_a, head, cntb, meanb, m2b);
+      epi_chunk_main<T, 32, HEAVY>(a, ev, r, n0, c, tbase + c, mean_a, rstd_a, head, cntb, meanb, m2b);
+    if (c < c_hi) epi_chunk_main<T, 16, HEAVY>(a, ev, r, n0, c, tbase + c, mean_a, rstd_a, head, cntb, meanb, m2b);
   }
 
   if (fl & EPI_HEAD) {
@@ -510,7 +514,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& 
     if (a.head_out) st_global_f32_if(a.head_out + r.mc, r.mk * (head + a.head_b), r.valid && half == 0);
   }
 
-  if (fl & EPI_LN_B) {
+  if (HEAVY && (fl & EPI_LN_B)) {
     stats_combine(cntb, meanb, m2b, xme, xot, bar_id, half);
     const float rstd_b = rsqrtf(m2b / fmaxf(cntb, 1.f) + a.eps);
     tmem_wait_st();  // the parked values are in TMEM before they are read back
@@ -561,7 +565,7 @@ __device__ __forceinline__ void cpasync_chunk(const GemmArgs& a, const int32_t* 
   }
 }
 
-template <typename T>
+template <typename T, bool HEAVY>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_ws_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, int stages) {
@@ -796,7 +800,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
-        epilogue_tile<T>(a, ev, xch, bar_id, half, row, nt * a.bn, trow, lane);
+        epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, nt * a.bn, trow, lane);
       }
       tc_fence_before();
       __syncwarp();
