@@ -117,6 +117,22 @@ int make_tmap(CUtensorMap* m, const void* ptr, bool bf16, long long cols, long l
   return SB_OK;
 }
 
+// 2D row-major tensor map with an explicit element type, box and swizzle
+// (epilogue stores / residual loads of the TMA epilogue).
+int make_tmap_ex(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize, long long cols, long long rows,
+                 long long row_elems, int box_cols, int box_rows, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_elems * esize};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled (epilogue) failed (%d)", (int)r);
+  return SB_OK;
+}
+
 // Operand producer of the tensor-core GEMM: 0 = TMA (gather4 rows + 2D weight
 // tiles) whenever the shapes allow it, 1 = cp.async everywhere. Read once from
 // SHRIMP_B200_GEMM_PRODUCER ("tma" | "cpasync").
@@ -125,6 +141,17 @@ int producer_mode() {
   if (mode < 0) {
     const char* e = getenv("SHRIMP_B200_GEMM_PRODUCER");
     mode = (e && strcmp(e, "cpasync") == 0) ? 1 : 0;
+  }
+  return mode;
+}
+
+// Epilogue of identity-row GEMMs: 0 = TMA-staged stores (default), 1 = per-row
+// stores (SHRIMP_B200_EPILOGUE=lsu, for comparison runs).
+int epilogue_mode() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("SHRIMP_B200_EPILOGUE");
+    mode = (e && strcmp(e, "lsu") == 0) ? 1 : 0;
   }
   return mode;
 }
@@ -168,21 +195,49 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
     if (int s = make_tmap(&ma, a.A, bf16, a.lda, a.a_rows, a.lda, a.gidx ? 1 : kBlockM)) return s;
     if (int s = make_tmap(&mb, a.Bw, bf16, a.kpad, a.n_total, a.kpad, a.bn)) return s;
   }
-  const int stages = gemm_stages(a.bn, a.taps);
-  const int smem = gemm_smem_bytes(a.bn, stages, a.taps);
+  // TMA epilogue: identity rows (output row = GEMM row), whole 32-column
+  // chunks per half tile, no per-row head / 16-bit residual.
+  CUtensorMap m16, m32, m32b;
+  memset(&m16, 0, sizeof(m16));
+  memset(&m32, 0, sizeof(m32));
+  memset(&m32b, 0, sizeof(m32b));
+  a.tma_epi = a.use_tma && !a.gidx && (a.bn / 2) % 32 == 0 && !(a.flags & (EPI_HEAD | EPI_RES16)) &&
+              ((uintptr_t)a.out16 % 16 == 0) && ((uintptr_t)a.out32 % 16 == 0) && ((uintptr_t)a.out32b % 16 == 0) &&
+              (a.ld16 * 2) % 16 == 0 && (a.ld32 * 4) % 16 == 0 && (a.ld32b * 4) % 16 == 0 && epilogue_mode() == 0;
+  if (a.tma_epi) {
+    const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (a.flags & EPI_OUT16)
+      if (int s = make_tmap_ex(&m16, a.out16, dt16, 2, a.n_total, a.M, a.ld16, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        return s;
+    if (a.flags & (EPI_OUT32 | EPI_RESID))
+      if (int s = make_tmap_ex(&m32, a.out32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.n_total, a.M, a.ld32, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+        return s;
+    if (a.flags & EPI_OUT32B)
+      if (int s = make_tmap_ex(&m32b, a.out32b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.n_total, a.M, a.ld32b, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+        return s;
+  }
+  const int stages = gemm_stages(a.bn, a.taps, a.tma_epi);
+  const int smem = gemm_smem_bytes(a.bn, stages, a.taps, a.tma_epi);
   const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B)) != 0;
-  const void* fn = heavy ? reinterpret_cast<const void*>(gemm_ws_kernel<T, true>)
-                         : reinterpret_cast<const void*>(gemm_ws_kernel<T, false>);
-  if (int s = ensure_smem(fn, smem)) return s;
+  const int variant = (heavy ? 1 : 0) + (a.tma_epi ? 2 : 0);
+  const void* fns[4] = {reinterpret_cast<const void*>(gemm_ws_kernel<T, false, false>),
+                        reinterpret_cast<const void*>(gemm_ws_kernel<T, true, false>),
+                        reinterpret_cast<const void*>(gemm_ws_kernel<T, false, true>),
+                        reinterpret_cast<const void*>(gemm_ws_kernel<T, true, true>)};
+  if (int s = ensure_smem(fns[variant], smem)) return s;
   const long long tiles = cdiv(a.M, kBlockM) * (a.n_total / a.bn);
   const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-  if (heavy)
-    gemm_ws_kernel<T, true><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, stages);
-  else
-    gemm_ws_kernel<T, false><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, stages);
+  switch (variant) {
+    case 0: gemm_ws_kernel<T, false, false><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, m16, m32, m32b, stages); break;
+    case 1: gemm_ws_kernel<T, true, false><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, m16, m32, m32b, stages); break;
+    case 2: gemm_ws_kernel<T, false, true><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, m16, m32, m32b, stages); break;
+    default: gemm_ws_kernel<T, true, true><<<grid, kGemmThreads, smem, st>>>(a, ma, mb, m16, m32, m32b, stages);
+  }
   if (sync_debug())
-    fprintf(stderr, "[sb] gemm M=%d N=%d bn=%d kpad=%d taps=%d cin=%d tma=%d stages=%d smem=%d grid=%d flags=%d\n",
-            a.M, a.n_total, a.bn, a.kpad, a.taps, a.cin, a.use_tma, stages, smem, grid, a.flags);
+    fprintf(stderr, "[sb] gemm M=%d N=%d bn=%d kpad=%d taps=%d cin=%d tma=%d tma_epi=%d stages=%d smem=%d grid=%d "
+            "flags=%d\n", a.M, a.n_total, a.bn, a.kpad, a.taps, a.cin, a.use_tma, a.tma_epi, stages, smem, grid, a.flags);
   return check_launch("gemm_ws_kernel");
 }
 

@@ -98,6 +98,7 @@ struct GemmArgs {
   int seq_len;             // rows per position in the seq layout (for EPI_LNB_TOKENS)
   int ntok;
   int* err;                // device status word
+  int tma_epi;             // identity rows: epilogue stores / residual loads through TMA (set by the host)
 };
 
 constexpr int kBlockM = 128;
@@ -115,7 +116,6 @@ constexpr int kMaxStages = 8;
 
 __host__ __device__ constexpr int gemm_stage_bytes(int bn) { return kTileABytes + bn * 128; }
 __host__ __device__ constexpr int gemm_gidx_bytes(int taps) { return 2 * kBlockM * taps * 4; }
-__host__ __device__ constexpr int gemm_smem_bytes(int bn, int stages, int taps);
 
 template <typename T>
 __device__ __forceinline__ void load16(const void* base, long long off, float (&v)[16]) {
@@ -198,13 +198,17 @@ constexpr int kEpiVecFloats = 1024 + 6 * 256;   // bias (n_total) + six N-vector
 constexpr int kEpiXchBytes = 4 * 2 * 32 * 16;    // [quadrant][half][row] float4
 constexpr int kEpiSmemBytes = kEpiVecFloats * 4 + kEpiXchBytes;
 
-__host__ __device__ constexpr int gemm_smem_bytes(int bn, int stages, int taps) {
-  return 1024 + stages * gemm_stage_bytes(bn) + gemm_gidx_bytes(taps) + kEpiSmemBytes + 8 * (2 * stages + 4) + 16;
+// TMA epilogue staging: kEpiWarps x (4 KB fp32 + 2 KB f16), 1024-aligned, plus
+// one residual-load mbarrier per epilogue warp.
+constexpr int kEpiTmaBytes = 8 * 6144;
+__host__ __device__ constexpr int gemm_smem_bytes(int bn, int stages, int taps, bool tma_epi = false) {
+  return 1024 + stages * gemm_stage_bytes(bn) + gemm_gidx_bytes(taps) + kEpiSmemBytes +
+         (tma_epi ? (kEpiTmaBytes + 1024) : 0) + 8 * (2 * stages + 4 + 8) + 16;
 }
 // Stages that fit next to the gather-index double buffer and the epilogue data.
-__host__ __device__ constexpr int gemm_stages(int bn, int taps) {
+__host__ __device__ constexpr int gemm_stages(int bn, int taps, bool tma_epi = false) {
   int s = kMaxStages;
-  while (s > 2 && gemm_smem_bytes(bn, s, taps) > 227 * 1024) --s;
+  while (s > 2 && gemm_smem_bytes(bn, s, taps, tma_epi) > 227 * 1024) --s;
   return s;
 }
 
@@ -524,6 +528,177 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& 
   }
 }
 
+// ---- TMA epilogue (identity-row GEMMs: output row = GEMM row) -------------------
+// Each epilogue warp stages a 32-row x 32-column chunk of its rows in shared
+// memory in the TMA's swizzled layout (fp32: 128-byte rows, 128B swizzle; f16:
+// 64-byte rows, 64B swizzle) and one lane writes it with a bulk tensor store;
+// the fp32 residual chunk arrives the same way (TMA load into the fp32
+// staging, overwritten in place by the new values). Rows past the tensor are
+// neither read nor written by the TMA unit.
+constexpr int kEpiStageBytes = 4096 + 2048;  // per epilogue warp: fp32 chunk + f16 chunk
+
+struct EpiTma {
+  const CUtensorMap* o16;
+  const CUtensorMap* o32;
+  const CUtensorMap* o32b;
+  uint8_t* st32;      // 4 KB, 1024-aligned
+  uint8_t* st16;      // 2 KB, 1024-aligned
+  uint32_t rbar;      // residual-load mbarrier of this warp
+};
+
+__device__ __forceinline__ uint32_t st32_addr(int r, int i4) { return r * 128 + (((i4) ^ (r & 7)) << 4); }
+__device__ __forceinline__ uint32_t st16_addr(int r, int i8) { return r * 64 + (((i8) ^ ((r >> 1) & 3)) << 4); }
+
+__device__ __forceinline__ void stage_row32(uint8_t* st, int r, const float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    *reinterpret_cast<float4*>(st + st32_addr(r, i)) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+__device__ __forceinline__ void unstage_row32(const uint8_t* st, int r, float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = *reinterpret_cast<const float4*>(st + st32_addr(r, i));
+    v[4 * i] = f.x;
+    v[4 * i + 1] = f.y;
+    v[4 * i + 2] = f.z;
+    v[4 * i + 3] = f.w;
+  }
+}
+template <typename T>
+__device__ __forceinline__ void stage_row16(uint8_t* st, int r, const float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u;
+    T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(v[8 * i + e]);
+    *reinterpret_cast<uint4*>(st + st16_addr(r, i)) = u;
+  }
+}
+
+// Make this warp's staged rows visible to the TMA unit and store them.
+__device__ __forceinline__ void stage_flush(const EpiTma& e, int lane, bool s32, const CUtensorMap* m32, bool s16,
+                                            int col, int row) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (s32) tma_store_2d(m32, col, row, smem_u32(e.st32));
+    if (s16) tma_store_2d(e.o16, col, row, smem_u32(e.st16));
+    bulk_commit();
+  }
+}
+// Before the staging is written again: the previous stores have read it.
+__device__ __forceinline__ void stage_reuse(int lane) {
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
+}
+
+template <typename T, bool HEAVY>
+__device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const EpiVecs& ev, const EpiTma& e,
+                                                  uint32_t& rphase, bool& ok, float4* xch, int bar_id, int half,
+                                                  const EpiRow& r, int m_first, int n0, uint32_t tbase, int lane) {
+  const int fl = HEAVY ? a.flags : (a.flags & ~(EPI_RESID | EPI_RES16 | EPI_LN_B));
+  const int hw = a.bn >> 1;                     // columns per half (a multiple of 32 here)
+  const int c_lo = half * hw, c_hi = c_lo + hw;
+  float4* xme = xch + half * 32 + lane;
+  const float4* xot = xch + (half ^ 1) * 32 + lane;
+
+  float mean_a = 0.f, rstd_a = 1.f;
+  if (fl & EPI_LN_A) {
+    float cnt = 0.f, mean = 0.f, m2 = 0.f;
+    for (int c = c_lo; c < c_hi; c += 32) {
+      float v[32], t[32];
+      tmem_ld32(tbase + c, v);
+      ld_vec<32>(ev.bias + n0 + c, t);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += t[i];
+      stats_merge_w<32>(cnt, mean, m2, v);
+    }
+    stats_combine(cnt, mean, m2, xme, xot, bar_id, half);
+    mean_a = mean;
+    rstd_a = rsqrtf(m2 / cnt + a.eps);
+  }
+
+  float cntb = 0.f, meanb = 0.f, m2b = 0.f;
+  const bool lnb = HEAVY && (fl & EPI_LN_B);
+  for (int c = c_lo; c < c_hi; c += 32) {
+    float v[32], t[32], x[32];
+    stage_reuse(lane);
+    if (HEAVY && (fl & EPI_RESID)) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(e.rbar, 4096);
+        tma_load_2d(smem_u32(e.st32), e.o32, n0 + c, m_first, e.rbar);
+      }
+      const bool got = ok && mbar_wait(e.rbar, rphase);
+      ok = __all_sync(0xffffffffu, got) != 0;
+      rphase ^= 1u;
+      unstage_row32(e.st32, lane, x);
+    }
+    tmem_ld32(tbase + c, v);
+    ld_vec<32>(ev.bias + n0 + c, t);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += t[i];
+    if (fl & EPI_LN_A) {
+      float w[32];
+      ld_vec<32>(ev.lnaw + c, w);
+      ld_vec<32>(ev.lnab + c, t);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaf((v[i] - mean_a) * rstd_a, w[i], t[i]);
+    }
+    if (fl & EPI_RELU) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
+    }
+    if (fl & EPI_GELU) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+    }
+    if (fl & EPI_MASK) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= r.mk;
+    }
+    if (HEAVY && (fl & EPI_RESID)) {
+      ld_vec<32>(ev.gamma + c, t);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaf(v[i], t[i], x[i]);
+    }
+    if (fl & EPI_POST_RELU) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
+    }
+    if (lnb) {
+      stats_merge_w<32>(cntb, meanb, m2b, v);
+      tmem_stw<32>(tbase + c, v);  // parked for the LayerNorm B pass
+    }
+    const bool s32 = (fl & (EPI_RESID | EPI_OUT32)) != 0;
+    const bool s16 = (fl & EPI_OUT16) && !lnb;
+    if (s32) stage_row32(e.st32, lane, v);
+    if (s16) stage_row16<T>(e.st16, lane, v);
+    if (s32 || s16) stage_flush(e, lane, s32, e.o32, s16, n0 + c, m_first);
+  }
+
+  if (lnb) {
+    stats_combine(cntb, meanb, m2b, xme, xot, bar_id, half);
+    const float rstd_b = rsqrtf(m2b / fmaxf(cntb, 1.f) + a.eps);
+    tmem_wait_st();
+    for (int c = c_lo; c < c_hi; c += 32) {
+      float v[32], w[32], t[32];
+      stage_reuse(lane);
+      tmem_ld32(tbase + c, v);
+      ld_vec<32>(ev.lnbw + c, w);
+      ld_vec<32>(ev.lnbb + c, t);
+      // rows outside LayerNorm B (non-token rows with EPI_LNB_TOKENS) keep v
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = r.lnb_row ? fmaf((v[i] - meanb) * rstd_b, w[i], t[i]) : v[i];
+      const bool s32 = (fl & EPI_OUT32B) != 0;
+      const bool s16 = (fl & EPI_OUT16) != 0;
+      if (s32) stage_row32(e.st32, lane, v);
+      if (s16) stage_row16<T>(e.st16, lane, v);
+      if (s32 || s16) stage_flush(e, lane, s32, e.o32b, s16, n0 + c, m_first);
+    }
+  }
+}
+
 // cp.async producer for one K chunk (used when Cin is not a multiple of 64):
 // thread `pt` of the 128 producer threads copies 16-byte pieces of 8 A rows
 // and BN/16 B rows into the 128-byte-swizzled stage.
@@ -565,10 +740,12 @@ __device__ __forceinline__ void cpasync_chunk(const GemmArgs& a, const int32_t* 
   }
 }
 
-template <typename T, bool HEAVY>
+template <typename T, bool HEAVY, bool TMA_EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_ws_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_a,
-                   const __grid_constant__ CUtensorMap tmap_b, int stages) {
+                   const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_o16,
+                   const __grid_constant__ CUtensorMap tmap_o32, const __grid_constant__ CUtensorMap tmap_o32b,
+                   int stages) {
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -584,12 +761,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t epi_off = gidx_off + gemm_gidx_bytes(a.taps);
   float* vecs = reinterpret_cast<float*>(gbase + epi_off);             // epilogue vectors
   float4* xch_all = reinterpret_cast<float4*>(gbase + epi_off + kEpiVecFloats * 4);  // [4][2][32]
-  const uint32_t bar0 = base + epi_off + kEpiSmemBytes;
+  // TMA epilogue staging, 1024-aligned (present when a.tma_epi)
+  const uint32_t stg_off = (epi_off + kEpiSmemBytes + 1023u) & ~1023u;
+  const uint32_t bar0 = base + (a.tma_epi ? stg_off + kEpiTmaBytes : epi_off + kEpiSmemBytes);
   const uint32_t full_bar = bar0;                 // [S]
   const uint32_t empty_bar = bar0 + 8 * S;        // [S]
   const uint32_t accf_bar = bar0 + 16 * S;        // [2]
   const uint32_t acce_bar = accf_bar + 16;        // [2]
-  const uint32_t tmem_slot = acce_bar + 16;
+  const uint32_t rload_bar = acce_bar + 16;       // [8] residual loads of the TMA epilogue
+  const uint32_t tmem_slot = rload_bar + 64;
   volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
 
   const int acc_cols = (a.bn + 31) & ~31;
@@ -615,6 +795,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(accf_bar + 8 * i, 1);
       mbar_init(acce_bar + 8 * i, kEpiWarps);
     }
+    for (int i = 0; i < kEpiWarps; ++i) mbar_init(rload_bar + 8 * i, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     if (tma) {
       prefetch_tmap(&tmap_a);
@@ -782,6 +963,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     const EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768,
                      vecs + 1024 + 1024, vecs + 1024 + 1280};
+    const EpiTma etma{&tmap_o16, &tmap_o32, &tmap_o32b, gbase + stg_off + warp * 6144,
+                      gbase + stg_off + warp * 6144 + 4096, rload_bar + 8 * warp};
+    uint32_t rphase = 0;
     int j = 0;
     EpiRow row = make_epi_row(a, (blockIdx.x / n_tiles) * kBlockM + quad * 32, quad * 32, kBlockM, lane);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
@@ -800,13 +984,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
-        epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, nt * a.bn, trow, lane);
+        if constexpr (TMA_EPI)
+          epilogue_tile_tma<T, HEAVY>(a, ev, etma, rphase, ok, xch, bar_id, half, row,
+                                      (t / n_tiles) * kBlockM + quad * 32, nt * a.bn, trow, lane);
+        else
+          epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, nt * a.bn, trow, lane);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar + 8 * ab);
       row = row_next;
     }
+    if (TMA_EPI && lane == 0) bulk_wait_all();  // the staging stays valid until the stores completed
+    __syncwarp();
   }
 
   if (!ok && a.err) atomicOr(a.err, 1);
