@@ -133,6 +133,22 @@ int make_tmap_ex(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int es
   return SB_OK;
 }
 
+// 3D map (columns, rows of a block, blocks) over a row-major buffer whose
+// blocks of `rows` rows follow each other; box {32 columns, 32 rows, 1 block}.
+int make_tmap_3d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize, long long cols, long long rows,
+                 long long blocks, long long row_elems, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)blocks};
+  cuuint64_t strides[2] = {(cuuint64_t)row_elems * esize, (cuuint64_t)(row_elems * rows) * esize};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled (3D) failed (%d)", (int)r);
+  return SB_OK;
+}
+
 // Operand producer of the tensor-core GEMM: 0 = TMA (gather4 rows + 2D weight
 // tiles) whenever the shapes allow it, 1 = cp.async everywhere. Read once from
 // SHRIMP_B200_GEMM_PRODUCER ("tma" | "cpasync").
@@ -253,12 +269,15 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
       xrows < cells)
     return 1;
   if (a.lda != C || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16 || producer_mode() == 1) return 1;
-  int ppt = kBlockM / cells;
-  while (ppt > 1 && ppt * xrows > 256) --ppt;
-  if (ppt * xrows > 256) return 1;
+  // positions per tile: 4, 2 or 1 (each position owns 128 / ppt TMEM lanes)
+  int ppt = 4;
+  while (ppt > 1 && (cells > kBlockM / ppt || ppt * xrows > 256)) ppt >>= 1;
+  if (cells > kBlockM / ppt || ppt * xrows > 256) return 1;
   const int win_rows = ppt * xrows;
-  const int stages = conv_ts_stages(C, win_rows);
-  const int smem = conv_ts_smem_bytes(C, stages, win_rows);
+  const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B)) != 0;
+  if (heavy && (a.flags & (EPI_RES16 | EPI_OUT32B | EPI_HEAD))) return 1;  // not in the TMA epilogue
+  const int stages = conv_ts_stages(C, win_rows, heavy);
+  const int smem = conv_ts_smem_bytes(C, stages, win_rows, heavy);
   if (smem > 227 * 1024) return 1;
   if (a.M <= 0 || npos <= 0) return SB_OK;
   a.bn = C;
@@ -269,17 +288,30 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
   memset(&mw, 0, sizeof(mw));
   if (int s = make_tmap(&mx, a.A, bf16, C, (long long)npos * xrows, C, win_rows)) return s;
   if (int s = make_tmap(&mw, a.Bw, bf16, a.kpad, C, a.kpad, C)) return s;
-  const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B)) != 0;
+  // heavy epilogue: TMA stores / residual loads through 3D maps (columns,
+  // rows of a position's block, positions): rows past a block are clipped
+  CUtensorMap m16, m32;
+  memset(&m16, 0, sizeof(m16));
+  memset(&m32, 0, sizeof(m32));
+  if (heavy) {
+    if ((uintptr_t)a.out16 % 16 || (uintptr_t)a.out32 % 16 || (a.ld16 * 2) % 16 || (a.ld32 * 4) % 16) return 1;
+    const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (a.flags & EPI_OUT16)
+      if (int s = make_tmap_3d(&m16, a.out16, dt16, 2, C, xrows, npos, a.ld16, CU_TENSOR_MAP_SWIZZLE_64B)) return s;
+    if (int s = make_tmap_3d(&m32, a.out32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, xrows, npos, a.ld32,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return s;
+  }
   const void* fn = heavy ? reinterpret_cast<const void*>(conv_ts_kernel<T, true>)
                          : reinterpret_cast<const void*>(conv_ts_kernel<T, false>);
   if (int s = ensure_smem(fn, smem)) return s;
-  ConvTsGeom geo{ppt, cells, xrows, npos};
+  ConvTsGeom geo{ppt, cells, xrows, npos, xrows - cells};
   const int tiles = (npos + ppt - 1) / ppt;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   if (heavy)
-    conv_ts_kernel<T, true><<<grid, kConvThreads, smem, st>>>(a, geo, mx, mw, stages);
+    conv_ts_kernel<T, true><<<grid, kConvThreads, smem, st>>>(a, geo, mx, mw, m16, m32, stages);
   else
-    conv_ts_kernel<T, false><<<grid, kConvThreads, smem, st>>>(a, geo, mx, mw, stages);
+    conv_ts_kernel<T, false><<<grid, kConvThreads, smem, st>>>(a, geo, mx, mw, m16, m32, stages);
   if (sync_debug())
     fprintf(stderr, "[sb] conv_ts M=%d C=%d ppt=%d win=%d stages=%d smem=%d grid=%d flags=%d\n", a.M, C, ppt,
             win_rows, stages, smem, grid, a.flags);

@@ -220,45 +220,36 @@ __device__ __forceinline__ float decode_bins(const float* logits) {
 }
 
 // Two-layer head over cat(token a, token b, masked mean of cells):
-// value_head(relu(value_reduction(.))) (model.py:990-1003). Every thread
-// works: layer 1 gives thread t output channel t % C for the positions
-// t / C, t / C + G, ... (G = threads / C groups); layer 2 spreads the
-// (bin, position) pairs over the threads.
+// value_head(relu(value_reduction(.))) (model.py:990-1003).
 __device__ void heads_mlp(const float* vin, int C, const float* wT, const float* bias, const float* hwT,
                           const float* hbias, float* hidden, float* logits_s, int npos) {
   const int tid = threadIdx.x;
-  const int groups = max(1, kHeadsThreads / C);
-  for (int j0 = 0; j0 < C; j0 += kHeadsThreads / groups) {
-    const int j = j0 + tid % (kHeadsThreads / groups);
-    const int g = tid / (kHeadsThreads / groups);
-    if (j < C && g < groups) {
-      constexpr int kMaxPer = kHeadsPos;
-      float acc[kMaxPer];
+  for (int j = tid; j < C; j += kHeadsThreads) {
+    float acc[kHeadsPos];
 #pragma unroll
-      for (int q = 0; q < kMaxPer; ++q) acc[q] = 0.f;
-      for (int k = 0; k < 3 * C; ++k) {
-        const float w = __ldg(wT + (long long)k * C + j);
+    for (int p = 0; p < kHeadsPos; ++p) acc[p] = 0.f;
+    for (int k = 0; k < 3 * C; ++k) {
+      const float w = __ldg(wT + (long long)k * C + j);
 #pragma unroll
-        for (int q = 0; q < kMaxPer; ++q) {
-          const int p = g + q * groups;
-          if (p < kHeadsPos) acc[q] = fmaf(w, vin[p * 3 * C + k], acc[q]);
-        }
-      }
-      const float bj = __ldg(bias + j);
-#pragma unroll
-      for (int q = 0; q < kMaxPer; ++q) {
-        const int p = g + q * groups;
-        if (p < kHeadsPos) hidden[p * C + j] = fmaxf(acc[q] + bj, 0.f);
-      }
+      for (int p = 0; p < kHeadsPos; ++p) acc[p] = fmaf(w, vin[p * 3 * C + k], acc[p]);
     }
+    const float bj = __ldg(bias + j);
+#pragma unroll
+    for (int p = 0; p < kHeadsPos; ++p) hidden[p * C + j] = fmaxf(acc[p] + bj, 0.f);
   }
   __syncthreads();
-  for (int idx = tid; idx < kBins * kHeadsPos; idx += kHeadsThreads) {
-    const int p = idx / kBins, o = idx - p * kBins;
-    float acc = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < C; ++j) acc = fmaf(__ldg(hwT + (long long)j * kBins + o), hidden[p * C + j], acc);
-    logits_s[p * kBins + o] = acc + __ldg(hbias + o);
+  for (int o = tid; o < kBins; o += kHeadsThreads) {
+    float acc[kHeadsPos];
+#pragma unroll
+    for (int p = 0; p < kHeadsPos; ++p) acc[p] = 0.f;
+    for (int j = 0; j < C; ++j) {
+      const float w = __ldg(hwT + (long long)j * kBins + o);
+#pragma unroll
+      for (int p = 0; p < kHeadsPos; ++p) acc[p] = fmaf(w, hidden[p * C + j], acc[p]);
+    }
+    const float bo = __ldg(hbias + o);
+#pragma unroll
+    for (int p = 0; p < kHeadsPos; ++p) logits_s[p * kBins + o] = acc[p] + bo;
   }
   __syncthreads();
   (void)npos;

@@ -32,22 +32,27 @@ constexpr int kConvMaxStages = 8;
 constexpr int kConvStageChunks = 2;  // 64-wide K chunks per ring stage (one barrier round trip per 8 MMAs)
 
 struct ConvTsGeom {
-  int ppt;        // positions per tile
-  int cells;      // output rows per position
+  int ppt;        // positions per tile (1, 2 or 4)
+  int cells;      // output rows per position (<= 128 / ppt)
   int xrows;      // X rows per position (window rows = ppt * xrows)
   int npos;       // positions
+  int tokoff;     // output rows before the cells in each position's block (seq layout: 8 tokens)
 };
+// TMEM lane (tile row) r holds cell r % lpb of the tile's position r / lpb,
+// lpb = 128 / ppt lanes per position: each 32-lane quadrant covers one
+// contiguous run of one position's rows (lanes past `cells` are padding).
 
 __host__ __device__ constexpr int conv_win_box_bytes(int win_rows) { return (win_rows * 128 + 1023) / 1024 * 1024; }
-__host__ __device__ constexpr int conv_ts_smem_bytes(int c, int stages, int win_rows) {
+// tma_epi: the epilogue stages its chunks for TMA stores (residual convs).
+__host__ __device__ constexpr int conv_ts_smem_bytes(int c, int stages, int win_rows, bool tma_epi = false) {
   return 1024 + stages * kConvStageChunks * c * 128 + 2 * (c / 64) * conv_win_box_bytes(win_rows) + kEpiSmemBytes +
-         8 * (2 * stages + 8) + 16;
+         (tma_epi ? kEpiTmaBytes + 1024 : 0) + 8 * (2 * stages + 8 + 8) + 16;
 }
 // Ring depth: limited by shared memory and by TMEM (two C-column accumulators
 // plus 32 columns per A chunk of each stage, within 512 columns).
-__host__ __device__ constexpr int conv_ts_stages(int c, int win_rows) {
+__host__ __device__ constexpr int conv_ts_stages(int c, int win_rows, bool tma_epi = false) {
   int s = kConvMaxStages;
-  while (s > 2 && (conv_ts_smem_bytes(c, s, win_rows) > 227 * 1024 ||
+  while (s > 2 && (conv_ts_smem_bytes(c, s, win_rows, tma_epi) > 227 * 1024 ||
                    2 * ((c + 31) / 32 * 32) + 32 * kConvStageChunks * s > 512))
     --s;
   return s;
@@ -56,7 +61,8 @@ __host__ __device__ constexpr int conv_ts_stages(int c, int win_rows) {
 template <typename T, bool HEAVY>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv_ts_kernel(const GemmArgs a, const ConvTsGeom geo, const __grid_constant__ CUtensorMap tmap_x,
-                   const __grid_constant__ CUtensorMap tmap_w, int stages) {
+                   const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_o16,
+                   const __grid_constant__ CUtensorMap tmap_o32, int stages) {
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -66,7 +72,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const int nbox = C / 64;
   const int win_rows = geo.ppt * geo.xrows;
   const int box_bytes = conv_win_box_bytes(win_rows);
-  const int tile_rows = geo.ppt * geo.cells;
+  const int lpb = kBlockM / geo.ppt;  // TMEM lanes per position
 
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -77,7 +83,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const uint32_t epi_off = win_off + 2 * nbox * box_bytes;
   float* vecs = reinterpret_cast<float*>(gbase + epi_off);
   float4* xch_all = reinterpret_cast<float4*>(gbase + epi_off + kEpiVecFloats * 4);
-  const uint32_t bar0 = base + epi_off + kEpiSmemBytes;
+  // TMA epilogue staging (heavy instantiation), 1024-aligned
+  const uint32_t stg_off = (epi_off + kEpiSmemBytes + 1023u) & ~1023u;
+  const uint32_t bar0 = base + (HEAVY ? stg_off + kEpiTmaBytes : epi_off + kEpiSmemBytes);
   // Stage s = weight chunk in shared memory + A chunk in TMEM slot s: full
   // when the TMA bytes landed and the four A builders stored their rows;
   // empty when the MMAs that read both completed.
@@ -87,7 +95,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const uint32_t wine_bar = winf_bar + 16;                // [2]   window consumed
   const uint32_t accf_bar = wine_bar + 16;                // [2]
   const uint32_t acce_bar = accf_bar + 16;                // [2]
-  const uint32_t tmem_slot = acce_bar + 16;
+  const uint32_t rload_bar = acce_bar + 16;               // [8] residual loads (TMA epilogue)
+  const uint32_t tmem_slot = rload_bar + 64;
   volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
 
   const int acc_cols = (C + 31) & ~31;
@@ -113,6 +122,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       mbar_init(accf_bar + 8 * i, 1);
       mbar_init(acce_bar + 8 * i, kEpiWarps);
     }
+    for (int i = 0; i < kEpiWarps; ++i) mbar_init(rload_bar + 8 * i, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_w);
@@ -171,9 +181,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     uint32_t ac = 0;                  // A chunks produced
     int j = 0;
     // this thread's 7 tap rows for tile t (window-local, -1 = zero)
+    const int rp = row / lpb, ri = row - rp * lpb;  // position in the tile, cell in the position
     auto load_src = [&](int t, int (&src)[7]) {
-      const int m = t * tile_rows + row;
-      const bool live = row < tile_rows && m < a.M && t < tiles;
+      const int pos = t * geo.ppt + rp;
+      const int m = pos * geo.cells + ri;
+      const bool live = ri < geo.cells && pos < geo.npos && m < a.M && t < tiles;
       const int w0 = t * geo.ppt * geo.xrows;
 #pragma unroll
       for (int k = 0; k < 7; ++k) {
@@ -313,12 +325,29 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     const EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768,
                      vecs + 1024 + 1024, vecs + 1024 + 1280};
+    // this thread's row context for tile t (position-block row mapping)
+    const int r_in = quad * 32 + lane;
+    const int rp = r_in / lpb, ri = r_in - rp * lpb;
+    auto conv_row = [&](int t) {
+      EpiRow er;
+      const int pos = t * geo.ppt + rp;
+      const int m = pos * geo.cells + ri;
+      er.valid = ri < geo.cells && pos < geo.npos && m < a.M;
+      er.mc = er.valid ? m : a.M - 1;
+      er.orow = a.orow_from_gidx ? (long long)__ldg(a.gidx + (long long)er.mc * 7) : (long long)er.mc;
+      er.mk = ((a.flags & (EPI_MASK | EPI_HEAD)) && a.rowmask) ? __ldg(a.rowmask + er.orow) : 1.f;
+      er.lnb_row = (a.flags & EPI_LN_B) != 0;
+      if (a.flags & EPI_LNB_TOKENS) er.lnb_row = er.lnb_row && er.valid && (er.orow % a.seq_len) < a.ntok;
+      return er;
+    };
+    // quadrant -> (position, first cell) for the TMA boxes
+    const int qp = (quad * 32) / lpb, qi0 = quad * 32 - qp * lpb;
+    uint32_t rphase = 0;
     int j = 0;
-    EpiRow row = make_epi_row(a, blockIdx.x * tile_rows + quad * 32, quad * 32, tile_rows, lane);
+    EpiRow row = conv_row(blockIdx.x);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
       const int ab = j & 1;
-      const int tn = t + gridDim.x;  // next tile's rows: loads in flight during this tile
-      const EpiRow row_next = make_epi_row(a, tn * tile_rows + quad * 32, quad * 32, tile_rows, lane);
+      const EpiRow row_next = conv_row(t + gridDim.x);  // loads in flight during this tile
       const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (j >> 1) & 1);
       ok = __all_sync(0xffffffffu, got) != 0;
       ok = bar_red_and(bar_id, 64, ok);
@@ -326,13 +355,24 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       tc_fence_after();
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
-        epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, 0, trow, lane);
+        if constexpr (HEAVY) {
+          // rows of this quadrant: cells [qi0, qi0 + 32) of position t * ppt + qp, i.e. rows
+          // tokoff + qi0 ... of that position's block (the 3D maps clip past its end)
+          const EpiTma etma{&tmap_o16, &tmap_o32, &tmap_o32, gbase + stg_off + warp * 6144,
+                            gbase + stg_off + warp * 6144 + 4096, rload_bar + 8 * warp, t * geo.ppt + qp};
+          epilogue_tile_tma<T, HEAVY>(a, ev, etma, rphase, ok, xch, bar_id, half, row, geo.tokoff + qi0, 0, trow,
+                                      lane);
+        } else {
+          epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, 0, trow, lane);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar + 8 * ab);
       row = row_next;
     }
+    if (HEAVY && lane == 0) bulk_wait_all();  // the staging stays valid until the stores completed
+    __syncwarp();
   }
 
   if (!ok && a.err) atomicOr(a.err, 1);

@@ -544,7 +544,15 @@ struct EpiTma {
   uint8_t* st32;      // 4 KB, 1024-aligned
   uint8_t* st16;      // 2 KB, 1024-aligned
   uint32_t rbar;      // residual-load mbarrier of this warp
+  int z;              // < 0: 2D maps (col, row); else 3D maps (col, row, z)
 };
+
+__device__ __forceinline__ void tma_store_box(const EpiTma& e, const CUtensorMap* m, int col, int row, uint32_t src) {
+  if (e.z < 0)
+    tma_store_2d(m, col, row, src);
+  else
+    tma_store_3d(m, col, row, e.z, src);
+}
 
 __device__ __forceinline__ uint32_t st32_addr(int r, int i4) { return r * 128 + (((i4) ^ (r & 7)) << 4); }
 __device__ __forceinline__ uint32_t st16_addr(int r, int i8) { return r * 64 + (((i8) ^ ((r >> 1) & 3)) << 4); }
@@ -582,8 +590,8 @@ __device__ __forceinline__ void stage_flush(const EpiTma& e, int lane, bool s32,
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    if (s32) tma_store_2d(m32, col, row, smem_u32(e.st32));
-    if (s16) tma_store_2d(e.o16, col, row, smem_u32(e.st16));
+    if (s32) tma_store_box(e, m32, col, row, smem_u32(e.st32));
+    if (s16) tma_store_box(e, e.o16, col, row, smem_u32(e.st16));
     bulk_commit();
   }
 }
@@ -627,7 +635,10 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const EpiVe
     if (HEAVY && (fl & EPI_RESID)) {
       if (lane == 0) {
         mbar_arrive_expect_tx(e.rbar, 4096);
-        tma_load_2d(smem_u32(e.st32), e.o32, n0 + c, m_first, e.rbar);
+        if (e.z < 0)
+          tma_load_2d(smem_u32(e.st32), e.o32, n0 + c, m_first, e.rbar);
+        else
+          tma_load_3d(smem_u32(e.st32), e.o32, n0 + c, m_first, e.z, e.rbar);
       }
       const bool got = ok && mbar_wait(e.rbar, rphase);
       ok = __all_sync(0xffffffffu, got) != 0;
@@ -964,7 +975,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768,
                      vecs + 1024 + 1024, vecs + 1024 + 1280};
     const EpiTma etma{&tmap_o16, &tmap_o32, &tmap_o32b, gbase + stg_off + warp * 6144,
-                      gbase + stg_off + warp * 6144 + 4096, rload_bar + 8 * warp};
+                      gbase + stg_off + warp * 6144 + 4096, rload_bar + 8 * warp, -1};
     uint32_t rphase = 0;
     int j = 0;
     EpiRow row = make_epi_row(a, (blockIdx.x / n_tiles) * kBlockM + quad * 32, quad * 32, kBlockM, lane);
