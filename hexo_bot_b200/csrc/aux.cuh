@@ -219,97 +219,119 @@ __device__ __forceinline__ float decode_bins(const float* logits) {
   return fminf(fmaxf(sv / se, -1.f), 1.f);
 }
 
-// Two-layer head over cat(token a, token b, masked mean of cells):
-// value_head(relu(value_reduction(.))) (model.py:990-1003).
+// Value (and moves-left) heads over cat(token a, token b, masked mean of the
+// cells) of ln_final (model.py:931-1003): value_head(relu(value_reduction(.))),
+// then the binned decode (losses.py:40-61). One CTA = kHeadsPos positions,
+// 256 threads; activations are kept position-minor in shared memory
+// ([k][position]) so one 16-byte load gives four positions.
+// layer 1: thread t owns output channel t % C for 8 positions (t / C picks
+// which 8); layer 2: (bin, 4 positions) per thread.
 __device__ void heads_mlp(const float* vin, int C, const float* wT, const float* bias, const float* hwT,
-                          const float* hbias, float* hidden, float* logits_s, int npos) {
+                          const float* hbias, float* hidden, float* logits_s) {
   const int tid = threadIdx.x;
-  for (int j = tid; j < C; j += kHeadsThreads) {
-    float acc[kHeadsPos];
+  const int K = 3 * C;
+  const int groups = kHeadsPos / 8;  // 2 groups of 8 positions
+  for (int w0 = tid; w0 < C * groups; w0 += kHeadsThreads) {
+    const int j = w0 % C, g = w0 / C;
+    float acc[8];
 #pragma unroll
-    for (int p = 0; p < kHeadsPos; ++p) acc[p] = 0.f;
-    for (int k = 0; k < 3 * C; ++k) {
+    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < K; ++k) {
       const float w = __ldg(wT + (long long)k * C + j);
-#pragma unroll
-      for (int p = 0; p < kHeadsPos; ++p) acc[p] = fmaf(w, vin[p * 3 * C + k], acc[p]);
+      const float4 v0 = *reinterpret_cast<const float4*>(vin + k * kHeadsPos + g * 8);
+      const float4 v1 = *reinterpret_cast<const float4*>(vin + k * kHeadsPos + g * 8 + 4);
+      acc[0] = fmaf(w, v0.x, acc[0]);
+      acc[1] = fmaf(w, v0.y, acc[1]);
+      acc[2] = fmaf(w, v0.z, acc[2]);
+      acc[3] = fmaf(w, v0.w, acc[3]);
+      acc[4] = fmaf(w, v1.x, acc[4]);
+      acc[5] = fmaf(w, v1.y, acc[5]);
+      acc[6] = fmaf(w, v1.z, acc[6]);
+      acc[7] = fmaf(w, v1.w, acc[7]);
     }
     const float bj = __ldg(bias + j);
 #pragma unroll
-    for (int p = 0; p < kHeadsPos; ++p) hidden[p * C + j] = fmaxf(acc[p] + bj, 0.f);
+    for (int q = 0; q < 8; ++q) hidden[j * kHeadsPos + g * 8 + q] = fmaxf(acc[q] + bj, 0.f);
   }
   __syncthreads();
-  for (int o = tid; o < kBins; o += kHeadsThreads) {
-    float acc[kHeadsPos];
-#pragma unroll
-    for (int p = 0; p < kHeadsPos; ++p) acc[p] = 0.f;
+  for (int w0 = tid; w0 < kBins * (kHeadsPos / 4); w0 += kHeadsThreads) {
+    const int o = w0 % kBins, g = w0 / kBins;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
     for (int j = 0; j < C; ++j) {
       const float w = __ldg(hwT + (long long)j * kBins + o);
-#pragma unroll
-      for (int p = 0; p < kHeadsPos; ++p) acc[p] = fmaf(w, hidden[p * C + j], acc[p]);
+      const float4 h = *reinterpret_cast<const float4*>(hidden + j * kHeadsPos + g * 4);
+      acc[0] = fmaf(w, h.x, acc[0]);
+      acc[1] = fmaf(w, h.y, acc[1]);
+      acc[2] = fmaf(w, h.z, acc[2]);
+      acc[3] = fmaf(w, h.w, acc[3]);
     }
     const float bo = __ldg(hbias + o);
 #pragma unroll
-    for (int p = 0; p < kHeadsPos; ++p) logits_s[p * kBins + o] = acc[p] + bo;
+    for (int q = 0; q < 4; ++q) logits_s[(g * 4 + q) * kBins + o] = acc[q] + bo;
   }
   __syncthreads();
-  (void)npos;
 }
 
 __global__ void __launch_bounds__(kHeadsThreads) heads_kernel(const HeadsArgs a) {
   extern __shared__ float hsm[];
   const int C = a.C;
-  float* vin = hsm;                                   // [P][3C]
-  float* hidden = vin + kHeadsPos * 3 * C;            // [P][C]
-  float* logits = hidden + kHeadsPos * C;             // [P][65]
-  float* cnt = logits + kHeadsPos * kBins;            // [P]
+  float* vin = hsm;                                   // [3C][P]  (k-major, position-minor)
+  float* hidden = vin + 3 * C * kHeadsPos;            // [C][P]
+  float* logits = hidden + C * kHeadsPos;             // [P][65]
   const int b0 = blockIdx.x * kHeadsPos;
   const int npos = min(kHeadsPos, a.B - b0);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int npad = a.S - kNumTok;
 
-  if (tid < kHeadsPos) {
-    float c = 0.f;
-    if (tid < npos)
-      for (int n = 0; n < npad; ++n) c += a.rowmask[(long long)(b0 + tid) * a.S + kNumTok + n];
-    cnt[tid] = fmaxf(c, 1.f);
-  }
-  __syncthreads();
-  // pooled mean of ln_final cells (model.py:931-935)
-  for (int idx = tid; idx < kHeadsPos * C; idx += kHeadsThreads) {
-    const int p = idx / C, c = idx - p * C;
-    float s = 0.f;
-    if (p < npos) {
-      const long long base = (long long)(b0 + p) * a.S;
-#pragma unroll 8
-      for (int n = 0; n < npad; ++n) {
-        const long long row = base + kNumTok + n;
-        s = fmaf(__ldg(a.lnf32 + row * C + c), __ldg(a.rowmask + row), s);
+  // pooled mean of ln_final cells (model.py:931-935): one warp per position,
+  // four channels per lane per 16-byte load
+  for (int p = warp; p < kHeadsPos; p += kHeadsThreads / 32) {
+    const bool live = p < npos;
+    const long long base = (long long)(b0 + (live ? p : 0)) * a.S + kNumTok;
+    for (int c4 = lane * 4; c4 < C; c4 += 128) {
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      float cnt = 0.f;
+      if (live) {
+#pragma unroll 4
+        for (int n = 0; n < npad; ++n) {
+          const float mk = __ldg(a.rowmask + base + n);
+          const float4 v = __ldg(reinterpret_cast<const float4*>(a.lnf32 + (base + n) * C + c4));
+          s.x = fmaf(v.x, mk, s.x);
+          s.y = fmaf(v.y, mk, s.y);
+          s.z = fmaf(v.z, mk, s.z);
+          s.w = fmaf(v.w, mk, s.w);
+          cnt += mk;
+        }
       }
+      const float inv = 1.f / fmaxf(cnt, 1.f);
+      vin[(2 * C + c4) * kHeadsPos + p] = s.x * inv;
+      vin[(2 * C + c4 + 1) * kHeadsPos + p] = s.y * inv;
+      vin[(2 * C + c4 + 2) * kHeadsPos + p] = s.z * inv;
+      vin[(2 * C + c4 + 3) * kHeadsPos + p] = s.w * inv;
     }
-    vin[p * 3 * C + 2 * C + c] = s / cnt[p];
   }
   const int passes = a.ml_logits ? 2 : 1;
   for (int pass = 0; pass < passes; ++pass) {
-    const int ta = pass == 0 ? 0 : 4;
+    const int ta = pass == 0 ? 0 : 4;  // summary-token rows of the head (model.py:1005-1009)
     for (int idx = tid; idx < kHeadsPos * 2 * C; idx += kHeadsThreads) {
       const int p = idx / (2 * C), c = idx - p * 2 * C;
       float v = 0.f;
       if (p < npos) {
         const long long row = (long long)(b0 + p) * a.S + ta + (c >= C ? 1 : 0);
-        v = a.lnf32[row * C + (c % C)];
+        v = __ldg(a.lnf32 + row * C + (c % C));
       }
-      vin[p * 3 * C + c] = v;
+      vin[c * kHeadsPos + p] = v;
     }
     __syncthreads();
     if (pass == 0)
-      heads_mlp(vin, C, a.vr_wT, a.vr_b, a.vh_wT, a.vh_b, hidden, logits, npos);
+      heads_mlp(vin, C, a.vr_wT, a.vr_b, a.vh_wT, a.vh_b, hidden, logits);
     else
-      heads_mlp(vin, C, a.mr_wT, a.mr_b, a.mh_wT, a.mh_b, hidden, logits, npos);
+      heads_mlp(vin, C, a.mr_wT, a.mr_b, a.mh_wT, a.mh_b, hidden, logits);
     float* lo = pass == 0 ? a.value_logits : a.ml_logits;
     float* dec = pass == 0 ? a.value : a.ml;
-    for (int idx = tid; idx < npos * kBins; idx += kHeadsThreads) {
-      lo[(long long)b0 * kBins + idx] = logits[idx];
-    }
+    for (int idx = tid; idx < npos * kBins; idx += kHeadsThreads) lo[(long long)b0 * kBins + idx] = logits[idx];
     if (dec && tid < npos) {
       const float e = decode_bins(logits + tid * kBins);
       dec[b0 + tid] = pass == 0 ? e : (e + 1.f) * 0.5f * 209.f;
