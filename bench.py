@@ -44,8 +44,8 @@ CONFIGS = {
 METRIC = "Shrimp positions/sec at batch 4096 (1/2/4/8 B200); p50 latency at batch 256"
 LATENCY_BATCHES = (1, 16, 64, 256, 1024)
 # dram bytes (read + write) of one dominant-kernel launch at the bench shape,
-# from the committed ncu capture (profiles/conv_gemm_main.md); None until captured.
-DOMINANT_TRAFFIC_BYTES = 99_334_144
+# from the committed ncu capture (profiles/conv_ts_main.md); None until captured.
+DOMINANT_TRAFFIC_BYTES = 89_898_496
 
 
 def load_peaks() -> dict:
@@ -442,7 +442,7 @@ def conv_roofline(model, dev_in, cfg, shard, npad, device, flush, steps=20, warm
     peaks = load_peaks()
     achieved = flops / (ms / 1e3) / 1e12
     return {
-        "kernel": "gemm_ws_kernel (7-tap gather-GEMM conv + LayerNorm/ReLU epilogue), timed via sb_hex_conv_ln",
+        "kernel": "conv_ts_kernel (position-windowed 7-tap conv + LayerNorm/ReLU epilogue), timed via sb_hex_conv_ln",
         "bound": "tensor",
         "achieved": round(achieved, 2),
         "peak": peaks["tflops"],
