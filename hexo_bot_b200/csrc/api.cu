@@ -12,6 +12,7 @@
 
 #include "../../include/shrimp_b200.h"
 #include "attention.cuh"
+#include "attention_geo.cuh"
 #include "aux.cuh"
 #include "gemm.cuh"
 #include "conv_ts.cuh"
@@ -168,6 +169,18 @@ int epilogue_mode() {
   if (mode < 0) {
     const char* e = getenv("SHRIMP_B200_EPILOGUE");
     mode = (e && strcmp(e, "lsu") == 0) ? 1 : 0;
+  }
+  return mode;
+}
+
+// Attention core for short sequences of head_dim 16: 0 = the geometry-cached
+// kernel (default), 1 = the general position-resident kernel
+// (SHRIMP_B200_ATTN=resident, for comparison runs).
+int attn_mode() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("SHRIMP_B200_ATTN");
+    mode = (e && strcmp(e, "resident") == 0) ? 1 : 0;
   }
   return mode;
 }
@@ -334,6 +347,37 @@ int launch_attention(AttnArgs a, cudaStream_t st) {
   if (a.table_rows <= 0 || a.table_rows > kMaxTableRows)
     return fail(SB_ERR_UNSUPPORTED, "attention: %d bias rows (1..%d supported)", a.table_rows, kMaxTableRows);
   const int dp = round_up(a.D, 16);
+  // Geometry-cached kernel: head_dim 16, whole 64-column boxes of heads,
+  // q | k | v as the column blocks of one row-major buffer.
+  if (attn_mode() == 0 && a.mode == BIAS_COORDS && a.D == kGeoD && a.H % 4 == 0 && a.S > a.ntok &&
+      a.S <= kGeoMaxS && 2 * (a.S - a.ntok) + a.S <= kGeoThreads && a.table_rows <= 255 && a.coords && a.lut) {
+    const long long C = (long long)a.H * a.D;
+    const T* q = reinterpret_cast<const T*>(a.q);
+    const AttnGeoLayout L = attn_geo_layout(a.S, a.H);
+    if (a.k == q + C && a.v == q + 2 * C && a.row_stride == 3 * C && a.head_stride == a.D &&
+        a.pos_stride == (long long)a.S * 3 * C && (uintptr_t)a.q % 16 == 0 && L.total <= 227 * 1024 &&
+        L.nj >= 8 && L.nj <= 10) {
+      if (a.B <= 0) return SB_OK;
+      CUtensorMap tm;
+      memset(&tm, 0, sizeof(tm));
+      if (int s = make_tmap(&tm, a.q, std::is_same<T, __nv_bfloat16>::value, 3 * C, (long long)a.B * a.S, 3 * C,
+                            a.S))
+        return s;
+      const int grid = a.B < num_sms() ? a.B : num_sms();
+#define SB_GEO_CASE(NJV)                                                                              \
+  case NJV:                                                                                           \
+    if (int s = ensure_smem(reinterpret_cast<const void*>(attn_geo_kernel<T, NJV>), L.total)) return s; \
+    attn_geo_kernel<T, NJV><<<(unsigned)grid, kGeoThreads, L.total, st>>>(a, tm);                     \
+    return check_launch("attn_geo_kernel");
+      switch (L.nj) {
+        SB_GEO_CASE(8)
+        SB_GEO_CASE(9)
+        SB_GEO_CASE(10)
+        default: break;
+      }
+#undef SB_GEO_CASE
+    }
+  }
   // Position-resident kernel when the per-position row table and the K/V of at
   // least one head fit in shared memory: the largest head group that allows
   // two CTAs per SM, else one CTA per SM. Longer sequences stream.
@@ -589,7 +633,7 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
       at.B = B; at.S = S; at.H = H; at.D = D; at.ntok = kNumTok;
       at.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
       at.mode = BIAS_COORDS; at.table = w.bias_table; at.table_rows = SB_BIAS_ROWS + 1;
-      at.coords = coords32; at.keymask = rowmask; at.lut = net->lut;
+      at.coords = coords32; at.keymask = rowmask; at.lut = net->lut; at.err = err;
       if (int s = launch_attention<__half>(at, st)) return s;
       // out_proj, gamma * mask residual; LN2 for the MLP (model.py:511-512)
       GemmArgs go = linear_args(o16, C, w.wo, C, w.bo);
@@ -634,9 +678,18 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
       h.mr_wT = net->ml_red_wT; h.mr_b = net->ml_red_b; h.mh_wT = net->ml_head_wT; h.mh_b = net->ml_head_b;
       h.ml_logits = out->ml_logits; h.ml = out->moves_left;
     }
-    const int smem = (kHeadsPos * 3 * C + kHeadsPos * C + kHeadsPos * kBins + kHeadsPos) * 4;
-    if (int s = ensure_smem(reinterpret_cast<const void*>(heads_kernel), smem)) return s;
-    heads_kernel<<<(unsigned)cdiv(B, kHeadsPos), kHeadsThreads, smem, st>>>(h);
+    // positions per CTA: 4, or 8 once four per CTA would take more than
+    // two waves (fewer re-reads of the layer-1 weights)
+    const int P = (cdiv(B, 4) > 2 * num_sms() && heads_smem_floats(C, 8) * 4 <= 113 * 1024) ? 8 : 4;
+    const int smem = heads_smem_floats(C, P) * 4;
+    const void* fn = P == 4 ? reinterpret_cast<const void*>(heads_kernel<4>)
+                            : reinterpret_cast<const void*>(heads_kernel<8>);
+    if (int s = ensure_smem(fn, smem)) return s;
+    const unsigned grid = (unsigned)cdiv(B, P);
+    if (P == 4)
+      heads_kernel<4><<<grid, kHeadsThreads, smem, st>>>(h);
+    else
+      heads_kernel<8><<<grid, kHeadsThreads, smem, st>>>(h);
     if (int s = check_launch("heads_kernel")) return s;
   }
   return SB_OK;

@@ -56,6 +56,7 @@ struct AttnArgs {
                             // are padding: skipped / written as zeros); nullptr = S
   const int32_t* offset_map;  // BIAS_OFFSET: [S][S]
   int group;              // heads staged per pass (set by the host)
+  int* err;               // device status word (SB_DEV_ERR_* bits), or nullptr
 };
 
 constexpr int kAttnThreads = 256;

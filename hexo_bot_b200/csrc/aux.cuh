@@ -202,8 +202,8 @@ struct HeadsArgs {
   float* ml_logits; float* ml;
 };
 
-constexpr int kHeadsPos = 16;     // positions per CTA
 constexpr int kHeadsThreads = 256;
+constexpr int kHeadsKC = 32;  // layer-1 weight rows per shared-memory chunk
 
 // softmax expectation over the 65 bins on linspace(-1, 1), clamped to [-1, 1]
 // (losses.py:40-51).
@@ -219,125 +219,219 @@ __device__ __forceinline__ float decode_bins(const float* logits) {
   return fminf(fmaxf(sv / se, -1.f), 1.f);
 }
 
-// Value (and moves-left) heads over cat(token a, token b, masked mean of the
-// cells) of ln_final (model.py:931-1003): value_head(relu(value_reduction(.))),
-// then the binned decode (losses.py:40-61). One CTA = kHeadsPos positions,
-// 256 threads; activations are kept position-minor in shared memory
-// ([k][position]) so one 16-byte load gives four positions.
-// layer 1: thread t owns output channel t % C for 8 positions (t / C picks
-// which 8); layer 2: (bin, 4 positions) per thread.
-__device__ void heads_mlp(const float* vin, int C, const float* wT, const float* bias, const float* hwT,
-                          const float* hbias, float* hidden, float* logits_s) {
-  const int tid = threadIdx.x;
-  const int K = 3 * C;
-  const int groups = kHeadsPos / 8;  // 2 groups of 8 positions
-  for (int w0 = tid; w0 < C * groups; w0 += kHeadsThreads) {
-    const int j = w0 % C, g = w0 / C;
-    float acc[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < K; ++k) {
-      const float w = __ldg(wT + (long long)k * C + j);
-      const float4 v0 = *reinterpret_cast<const float4*>(vin + k * kHeadsPos + g * 8);
-      const float4 v1 = *reinterpret_cast<const float4*>(vin + k * kHeadsPos + g * 8 + 4);
-      acc[0] = fmaf(w, v0.x, acc[0]);
-      acc[1] = fmaf(w, v0.y, acc[1]);
-      acc[2] = fmaf(w, v0.z, acc[2]);
-      acc[3] = fmaf(w, v0.w, acc[3]);
-      acc[4] = fmaf(w, v1.x, acc[4]);
-      acc[5] = fmaf(w, v1.y, acc[5]);
-      acc[6] = fmaf(w, v1.z, acc[6]);
-      acc[7] = fmaf(w, v1.w, acc[7]);
-    }
-    const float bj = __ldg(bias + j);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) hidden[j * kHeadsPos + g * 8 + q] = fmaxf(acc[q] + bj, 0.f);
-  }
-  __syncthreads();
-  for (int w0 = tid; w0 < kBins * (kHeadsPos / 4); w0 += kHeadsThreads) {
-    const int o = w0 % kBins, g = w0 / kBins;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-    for (int j = 0; j < C; ++j) {
-      const float w = __ldg(hwT + (long long)j * kBins + o);
-      const float4 h = *reinterpret_cast<const float4*>(hidden + j * kHeadsPos + g * 4);
-      acc[0] = fmaf(w, h.x, acc[0]);
-      acc[1] = fmaf(w, h.y, acc[1]);
-      acc[2] = fmaf(w, h.z, acc[2]);
-      acc[3] = fmaf(w, h.w, acc[3]);
-    }
-    const float bo = __ldg(hbias + o);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) logits_s[(g * 4 + q) * kBins + o] = acc[q] + bo;
-  }
-  __syncthreads();
+// Shared memory of heads_kernel<P> in floats, laid out as 16-byte aligned
+// pieces: layer-1 weight ring [kHeadsRing][KC][C], inputs [3C][P], hidden
+// [C][P], partial sums [max(2 P C, 3 * 65 * P, ns * C * P)], counts [2 P],
+// logits [P][65].
+constexpr int kHeadsRing = 4;  // weight chunks in flight per CTA
+__host__ __device__ constexpr int heads_max(int x, int y) { return x > y ? x : y; }
+__host__ __device__ constexpr int heads_red_floats(int C, int P) {
+  return heads_max(heads_max(2 * P * C, 3 * kBins * P), heads_max(kHeadsThreads / C, 1) * C * P);
+}
+__host__ __device__ constexpr int heads_smem_floats(int C, int P) {
+  return kHeadsRing * kHeadsKC * C + 3 * C * P + C * P + heads_red_floats(C, P) + 2 * P + P * kBins;
 }
 
-__global__ void __launch_bounds__(kHeadsThreads) heads_kernel(const HeadsArgs a) {
-  extern __shared__ float hsm[];
-  const int C = a.C;
-  float* vin = hsm;                                   // [3C][P]  (k-major, position-minor)
-  float* hidden = vin + 3 * C * kHeadsPos;            // [C][P]
-  float* logits = hidden + C * kHeadsPos;             // [P][65]
-  const int b0 = blockIdx.x * kHeadsPos;
-  const int npos = min(kHeadsPos, a.B - b0);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int npad = a.S - kNumTok;
+// Value (and moves-left) heads over cat(token a, token b, masked mean of the
+// cells) of ln_final (model.py:931-1003): value_head(relu(value_reduction(.))),
+// then the binned decode (losses.py:40-61). One CTA = P positions, 256
+// threads; activations are kept position-minor in shared memory ([k][p]) so
+// one 16-byte load gives four positions. The kernel runs once per forward, at
+// MCTS batch sizes too, so it is built for latency: pooling gives each warp
+// half of one position's rows and loads them in batches of 16 before adding
+// them; the layer-1 weights stream through a ring of cp.async chunks (three
+// in flight while one is used); the dot products are split over K across
+// thread groups and reduced in a fixed order.
+template <int P>
+__device__ void heads_pass(const HeadsArgs& a, int pass, float* sm, int b0, int npos) {
+  const int C = a.C, S = a.S, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = 3 * C;
+  float* wbuf = sm;                              // [ring][KC][C]
+  float* vin = wbuf + kHeadsRing * kHeadsKC * C; // [3C][P]
+  float* hidden = vin + 3 * C * P;               // [C][P]
+  float* red = hidden + C * P;                   // partial sums
+  float* redc = red + heads_red_floats(C, P);    // [2P] row counts of the pooling units
+  float* logits = redc + 2 * P;                  // [P][65]
+  const float* w1 = pass == 0 ? a.vr_wT : a.mr_wT;
+  const float* b1 = pass == 0 ? a.vr_b : a.mr_b;
+  const float* w2 = pass == 0 ? a.vh_wT : a.mh_wT;
+  const float* b2 = pass == 0 ? a.vh_b : a.mh_b;
+  const int nchunks = K / kHeadsKC;  // C is a multiple of 32, so K is a multiple of KC
+  auto load_chunk = [&](int ch) {
+    if (ch < nchunks) {
+      const float* src = w1 + (long long)ch * kHeadsKC * C;
+      float* dst = wbuf + (ch % kHeadsRing) * kHeadsKC * C;
+      for (int i = tid * 4; i < kHeadsKC * C; i += kHeadsThreads * 4) cp_async16(smem_u32(dst + i), src + i, 16u);
+    }
+    cp_async_commit();  // one group per chunk (empty past the end) keeps the wait count uniform
+  };
+  for (int ch = 0; ch < kHeadsRing - 1; ++ch) load_chunk(ch);  // in flight during pooling
 
-  // pooled mean of ln_final cells (model.py:931-935): one warp per position,
-  // four channels per lane per 16-byte load
-  for (int p = warp; p < kHeadsPos; p += kHeadsThreads / 32) {
-    const bool live = p < npos;
-    const long long base = (long long)(b0 + (live ? p : 0)) * a.S + kNumTok;
-    for (int c4 = lane * 4; c4 < C; c4 += 128) {
-      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-      float cnt = 0.f;
-      if (live) {
+  // ---- inputs: summary tokens (model.py:1005-1009) and the masked mean of
+  // the cells (model.py:931-935) ------------------------------------------
+  const int ta = pass == 0 ? 0 : 4;
+  for (int idx = tid; idx < P * 2 * C; idx += kHeadsThreads) {
+    const int c = idx / P, p = idx - c * P;  // consecutive threads: consecutive positions of one channel
+    float v = 0.f;
+    if (p < npos) v = __ldg(a.lnf32 + ((long long)(b0 + p) * S + ta + (c >= C ? 1 : 0)) * C + (c % C));
+    vin[idx] = v;
+  }
+  if (pass == 0) {  // the cell mean is shared by both heads (kept in vin[2C, 3C))
+    // unit u = (position u / 2, rows of parity u % 2); the split does not
+    // depend on P, so a position's sum is the same in any batch
+    const int npad = S - kNumTok;
+    for (int u = warp; u < 2 * P; u += kHeadsThreads / 32) {
+      const int p = u >> 1, part = u & 1;
+      const bool live = p < npos;
+      const long long base = (long long)(b0 + (live ? p : 0)) * S + kNumTok;
+      for (int c4 = lane; c4 < C / 4; c4 += 32) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        float cnt = 0.f;
+        if (live) {
+          for (int n0 = part; n0 < npad; n0 += 32) {
+            float4 v[16];
+            float mk[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const int n = n0 + 2 * q;
+              const bool in = n < npad;
+              mk[q] = in ? __ldg(a.rowmask + base + n) : 0.f;
+              v[q] = in ? __ldg(reinterpret_cast<const float4*>(a.lnf32 + (base + n) * C) + c4)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              s.x = fmaf(v[q].x, mk[q], s.x);
+              s.y = fmaf(v[q].y, mk[q], s.y);
+              s.z = fmaf(v[q].z, mk[q], s.z);
+              s.w = fmaf(v[q].w, mk[q], s.w);
+              cnt += mk[q];
+            }
+          }
+        }
+        *reinterpret_cast<float4*>(red + u * C + 4 * c4) = s;
+        if (c4 == lane && lane == 0) redc[u] = cnt;
+      }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < P * C; idx += kHeadsThreads) {
+      const int c = idx / P, p = idx - c * P;
+      const float v = red[(2 * p) * C + c] + red[(2 * p + 1) * C + c];
+      const float n = redc[2 * p] + redc[2 * p + 1];
+      vin[(2 * C + c) * P + p] = v / fmaxf(n, 1.f);
+    }
+  }
+
+  // ---- layer 1: hidden = relu(vin . W1 + b1), K split over `ns` groups -----
+  const int ns = C <= kHeadsThreads ? kHeadsThreads / C : 1;
+  const int j = tid % C, g1 = tid / C;
+  const bool act1 = g1 < ns;
+  float acc[P];
+#pragma unroll
+  for (int p = 0; p < P; ++p) acc[p] = 0.f;
+  for (int ch = 0; ch < nchunks; ++ch) {
+    load_chunk(ch + kHeadsRing - 1);  // into the slot freed at the end of the previous step
+    cp_async_wait<kHeadsRing - 1>();  // chunk ch landed (this thread's copies) ...
+    __syncthreads();                  // ... and everyone's; the pooled inputs are visible
+    if (act1) {
+      const float* wb = wbuf + (ch % kHeadsRing) * kHeadsKC * C;
+      const float* vk = vin + ch * kHeadsKC * P;
 #pragma unroll 4
-        for (int n = 0; n < npad; ++n) {
-          const float mk = __ldg(a.rowmask + base + n);
-          const float4 v = __ldg(reinterpret_cast<const float4*>(a.lnf32 + (base + n) * C + c4));
-          s.x = fmaf(v.x, mk, s.x);
-          s.y = fmaf(v.y, mk, s.y);
-          s.z = fmaf(v.z, mk, s.z);
-          s.w = fmaf(v.w, mk, s.w);
-          cnt += mk;
+      for (int kk = g1; kk < kHeadsKC; kk += ns) {
+        const float w = wb[kk * C + j];
+#pragma unroll
+        for (int p = 0; p < P; p += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(vk + kk * P + p);
+          acc[p] = fmaf(w, v.x, acc[p]);
+          acc[p + 1] = fmaf(w, v.y, acc[p + 1]);
+          acc[p + 2] = fmaf(w, v.z, acc[p + 2]);
+          acc[p + 3] = fmaf(w, v.w, acc[p + 3]);
         }
       }
-      const float inv = 1.f / fmaxf(cnt, 1.f);
-      vin[(2 * C + c4) * kHeadsPos + p] = s.x * inv;
-      vin[(2 * C + c4 + 1) * kHeadsPos + p] = s.y * inv;
-      vin[(2 * C + c4 + 2) * kHeadsPos + p] = s.z * inv;
-      vin[(2 * C + c4 + 3) * kHeadsPos + p] = s.w * inv;
     }
+    __syncthreads();  // slot ch % ring may be refilled
   }
-  const int passes = a.ml_logits ? 2 : 1;
-  for (int pass = 0; pass < passes; ++pass) {
-    const int ta = pass == 0 ? 0 : 4;  // summary-token rows of the head (model.py:1005-1009)
-    for (int idx = tid; idx < kHeadsPos * 2 * C; idx += kHeadsThreads) {
-      const int p = idx / (2 * C), c = idx - p * 2 * C;
-      float v = 0.f;
-      if (p < npos) {
-        const long long row = (long long)(b0 + p) * a.S + ta + (c >= C ? 1 : 0);
-        v = __ldg(a.lnf32 + row * C + (c % C));
+  if (act1)
+#pragma unroll
+    for (int p = 0; p < P; ++p) red[(g1 * C + j) * P + p] = acc[p];
+  __syncthreads();
+  for (int idx = tid; idx < C * P; idx += kHeadsThreads) {
+    const int jj = idx / P, p = idx - jj * P;
+    float v = __ldg(b1 + jj);
+    for (int g = 0; g < ns; ++g) v += red[(g * C + jj) * P + p];
+    hidden[jj * P + p] = fmaxf(v, 0.f);
+  }
+  __syncthreads();
+
+  // ---- layer 2: logits = hidden . W2 + b2, C split over 3 groups ------------
+  {
+    const int o = tid % kBins, g2 = tid / kBins;  // 3 groups of 65 threads
+    if (g2 < 3) {
+      float acc2[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) acc2[p] = 0.f;
+#pragma unroll 4
+      for (int jj = g2; jj < C; jj += 3) {
+        const float w = __ldg(w2 + (long long)jj * kBins + o);
+#pragma unroll
+        for (int p = 0; p < P; p += 4) {
+          const float4 h = *reinterpret_cast<const float4*>(hidden + jj * P + p);
+          acc2[p] = fmaf(w, h.x, acc2[p]);
+          acc2[p + 1] = fmaf(w, h.y, acc2[p + 1]);
+          acc2[p + 2] = fmaf(w, h.z, acc2[p + 2]);
+          acc2[p + 3] = fmaf(w, h.w, acc2[p + 3]);
+        }
       }
-      vin[c * kHeadsPos + p] = v;
+#pragma unroll
+      for (int p = 0; p < P; ++p) red[(g2 * kBins + o) * P + p] = acc2[p];
     }
-    __syncthreads();
-    if (pass == 0)
-      heads_mlp(vin, C, a.vr_wT, a.vr_b, a.vh_wT, a.vh_b, hidden, logits);
-    else
-      heads_mlp(vin, C, a.mr_wT, a.mr_b, a.mh_wT, a.mh_b, hidden, logits);
-    float* lo = pass == 0 ? a.value_logits : a.ml_logits;
-    float* dec = pass == 0 ? a.value : a.ml;
-    for (int idx = tid; idx < npos * kBins; idx += kHeadsThreads) lo[(long long)b0 * kBins + idx] = logits[idx];
-    if (dec && tid < npos) {
-      const float e = decode_bins(logits + tid * kBins);
-      dec[b0 + tid] = pass == 0 ? e : (e + 1.f) * 0.5f * 209.f;
-    }
-    __syncthreads();
   }
+  __syncthreads();
+  float* lo = pass == 0 ? a.value_logits : a.ml_logits;
+  for (int idx = tid; idx < P * kBins; idx += kHeadsThreads) {
+    const int p = idx / kBins, o = idx - p * kBins;
+    const float v = __ldg(b2 + o) + red[o * P + p] + red[(kBins + o) * P + p] + red[(2 * kBins + o) * P + p];
+    logits[idx] = v;
+    if (p < npos) lo[(long long)b0 * kBins + idx] = v;
+  }
+  __syncthreads();
+  // ---- binned decode: one warp per position ---------------------------------
+  float* dec = pass == 0 ? a.value : a.ml;
+  if (dec) {
+    for (int p = warp; p < npos; p += kHeadsThreads / 32) {
+      const float* l = logits + p * kBins;
+      float mx = -INFINITY;
+      for (int i = lane; i < kBins; i += 32) mx = fmaxf(mx, l[i]);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float se = 0.f, sv = 0.f;
+      for (int i = lane; i < kBins; i += 32) {
+        const float e = expf(l[i] - mx);
+        se += e;
+        sv += e * (-1.f + 2.f * (float)i / (float)(kBins - 1));
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        se += __shfl_xor_sync(0xffffffffu, se, o);
+        sv += __shfl_xor_sync(0xffffffffu, sv, o);
+      }
+      if (lane == 0) {
+        const float e = fminf(fmaxf(sv / se, -1.f), 1.f);
+        dec[b0 + p] = pass == 0 ? e : (e + 1.f) * 0.5f * 209.f;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // shared buffers are reused by the next pass
+}
+
+template <int P>
+__global__ void __launch_bounds__(kHeadsThreads) heads_kernel(const HeadsArgs a) {
+  extern __shared__ __align__(16) float hsm[];
+  const int b0 = blockIdx.x * P;
+  const int npos = min(P, a.B - b0);
+  heads_pass<P>(a, 0, hsm, b0, npos);
+  if (a.ml_logits) heads_pass<P>(a, 1, hsm, b0, npos);
 }
 
 __global__ void decode_binned_kernel(const float* logits, int B, float scale, float offset, float* out) {
