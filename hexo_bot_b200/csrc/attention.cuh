@@ -123,6 +123,8 @@ __device__ __forceinline__ void attn_score_tile(float (&out)[4], const uint32_t 
 template <typename T, int DP, int NT>
 __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
+  pdl_launch_dependents();
+  pdl_wait();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int S = a.S, D = a.D, G = a.group;
@@ -424,6 +426,8 @@ template <typename T, int DP>
 __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnArgs a) {
   using SM = AttnStreamSmem<DP>;
   extern __shared__ __align__(16) uint8_t smem[];
+  pdl_launch_dependents();
+  pdl_wait();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int qblk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;

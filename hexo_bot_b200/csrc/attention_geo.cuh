@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
   // ---- once per CTA: bias table (pre-divided by the softmax scale; rows past
   // the table, including the excluded-key row 255, are -inf), LUT, zero pad
   // rows of every box, barriers --------------------------------------------
+  pdl_launch_dependents();
   const float inv_scale = sqrtf((float)a.D);
   for (int i = tid; i < 256 * H; i += kGeoThreads) {
     const int r = i / H, h = i - r * H;
@@ -161,6 +162,7 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
     prefetch_tmap(&tmap);
   }
   __syncthreads();
+  pdl_wait();  // q, k, v, coordinates and the key mask come from earlier kernels
 
   auto issue = [&](int b, int buf) {  // thread 0
     const uint32_t bar = full0 + 8 * buf;

@@ -62,6 +62,8 @@ struct PrepArgs {
 // absolute-row gather table (tap 0 = self, taps 1..6 = DIRECTIONS neighbours;
 // reference trunk gather_idx, model.py:860-863), the row mask and int32 coords.
 __global__ void prep_cells_kernel(const PrepArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long ncell = (long long)a.B * a.npad;
   if (i < ncell) {
@@ -102,6 +104,8 @@ __global__ void prep_cells_kernel(const PrepArgs a) {
 // attention block's LN1 input (precomputed per weights).
 __global__ void init_tokens_kernel(const float* tokens, const __half* tokens_ln16, int B, int S, int C,
                                    float* seq32, __half* xa16) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long total = (long long)B * kNumTok * C;
   if (i >= total) return;
@@ -266,6 +270,7 @@ __device__ void heads_pass(const HeadsArgs& a, int pass, float* sm, int b0, int 
     cp_async_commit();  // one group per chunk (empty past the end) keeps the wait count uniform
   };
   for (int ch = 0; ch < kHeadsRing - 1; ++ch) load_chunk(ch);  // in flight during pooling
+  pdl_wait();  // ln_final and the row mask come from earlier kernels (weights do not)
 
   // ---- inputs: summary tokens (model.py:1005-1009) and the masked mean of
   // the cells (model.py:931-935) ------------------------------------------
@@ -428,6 +433,7 @@ __device__ void heads_pass(const HeadsArgs& a, int pass, float* sm, int b0, int 
 template <int P>
 __global__ void __launch_bounds__(kHeadsThreads) heads_kernel(const HeadsArgs a) {
   extern __shared__ __align__(16) float hsm[];
+  pdl_launch_dependents();
   const int b0 = blockIdx.x * P;
   const int npos = min(P, a.B - b0);
   heads_pass<P>(a, 0, hsm, b0, npos);

@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const int nk = a.kpad / kChunkK;  // 7 * C / 64 chunks per tile
   const int nst = (nk + kConvStageChunks - 1) / kConvStageChunks;  // ring stages per tile
 
+  pdl_launch_dependents();
   if (warp == kConvMmaWarp) {
     tmem_alloc(tmem_slot, ncols);
     tmem_relinquish();
@@ -132,6 +133,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
   bool ok = true;
+  // Roles that read activations or write global memory wait for the previous
+  // kernel; the weight producer and the MMA issuer (shared memory and TMEM
+  // only) start filling the weight ring during that wait.
+  if (warp != kConvWProducer && warp != kConvMmaWarp) pdl_wait();
 
   if (warp == kConvWinProducer) {
     // ------------------------------------------------------------ window producer

@@ -793,6 +793,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int nk = a.kpad / kChunkK;
   const bool tma = a.use_tma != 0;
 
+  pdl_launch_dependents();
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, ncols);
     tmem_relinquish();
@@ -818,6 +819,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
   bool ok = true;
+  // The epilogue reads and writes activations: it waits for the previous
+  // kernel. The MMA issuer touches shared memory and TMEM only. The producer
+  // waits before its first activation load (below).
+  if (warp < kMmaWarp) pdl_wait();
 
   if (warp >= kProducerWarp0) {
     // ------------------------------------------------------------ producers
@@ -827,6 +832,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else {
       uint32_t it = 0;
       int j = 0;
+      // The weights do not depend on the previous kernel: on the TMA path the
+      // B tiles of the first ring stages go out before the wait.
+      int pre = 0;
+      if (tma && (int)blockIdx.x < tiles) {
+        pre = S < nk ? S : nk;
+        if (lane == 0) {
+          const int n0 = (blockIdx.x % n_tiles) * a.bn;
+          for (int c = 0; c < pre; ++c) {
+            mbar_arrive_expect_tx(full_bar + 8 * c, kTileABytes + a.bn * 128);
+            tma_load_2d(base + c * stage_bytes + kTileABytes, &tmap_b, c * kChunkK, n0, full_bar + 8 * c);
+          }
+        }
+        __syncwarp();
+      }
+      pdl_wait();
       const int gwords = kBlockM * a.taps;
       // stage the gather rows of tile t into gather buffer `buf` (cp.async)
       auto fetch_gidx = [&](int t, int buf) {
@@ -874,7 +894,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int k0 = c * kChunkK;
             const int tap = k0 / a.cin;
             const int col = k0 - tap * a.cin;
-            if (lane == 0) mbar_arrive_expect_tx(full_bar + 8 * s, kTileABytes + a.bn * 128);
+            const bool b_sent = it < (uint32_t)pre;  // B tile already issued before the wait
+            if (lane == 0 && !b_sent) mbar_arrive_expect_tx(full_bar + 8 * s, kTileABytes + a.bn * 128);
             __syncwarp();
             if (a.gidx) {
               int rr[4];
@@ -888,7 +909,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               // contiguous rows: one 128-row box (rows past the end read as zeros)
               tma_load_2d(sA, &tmap_a, col, m0, full_bar + 8 * s);
             }
-            if (lane == 0) tma_load_2d(sB, &tmap_b, k0, n0, full_bar + 8 * s);
+            if (lane == 0 && !b_sent) tma_load_2d(sB, &tmap_b, k0, n0, full_bar + 8 * s);
           } else {
             cpasync_chunk<T>(a, gs, m0, n0, c, sA, sB, pt);
             cp_async_commit();

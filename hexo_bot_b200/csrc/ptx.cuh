@@ -18,6 +18,17 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---- programmatic dependent launch ----------------------------------------------
+// launch_dependents lets the next kernel of the stream (launched with the
+// programmatic-serialization attribute) begin its prologue on SMs this grid
+// frees; wait blocks until every earlier grid has completed and its memory is
+// visible. Every forward kernel waits before it reads an activation or writes
+// any global memory; without the attribute both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 // ---- cp.async (16-byte, L2-only, zero-fill when src_bytes == 0) -------------
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes)
