@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         if (lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
         break;
       }
-      const uint8_t* win = gbase + win_off + wb * nbox * box_bytes;
+      const uint32_t win = base + win_off + wb * nbox * box_bytes;  // shared-window address
       // gather chunk c of this thread's row from the window (zeros for a
       // missing tap) into 32 registers
       auto gather = [&](int c, uint32_t (&v)[32]) {
@@ -225,10 +225,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         // branch-free: a missing tap reads row 0 and is masked to zero
         const int rr = r < 0 ? 0 : r;
         const uint32_t keep = r < 0 ? 0u : 0xffffffffu;
-        const uint8_t* rowp = win + bx * box_bytes + rr * 128;
+        const uint32_t rowp = win + bx * box_bytes + rr * 128;
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
-          const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((p ^ (rr & 7)) << 4));
+          const uint4 u = lds128(rowp + ((p ^ (rr & 7)) << 4));
           v[4 * p] = u.x & keep;
           v[4 * p + 1] = u.y & keep;
           v[4 * p + 2] = u.z & keep;
