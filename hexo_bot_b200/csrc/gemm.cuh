@@ -182,7 +182,31 @@ __device__ __forceinline__ void stats_merge(float& cnt, float& mean, float& m2, 
   cnt = tot;
 }
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
+// Exact (erf) GELU, x * Phi(x), without erff: Phi(x) = 1 - h (x >= 0) or h
+// (x < 0) with h = 0.5 * exp(-z^2) * R(z), z = min(|x| / sqrt(2), 4), and R a
+// degree-11 polynomial fit of exp(z^2) * erfc(z) on [0, 4] (csrc/fit_gelu.py
+// produces the coefficients and checks the error: at most ~8e-7 absolute
+// against 0.5 * x * (1 + erf(x / sqrt(2))) over all float32 x). Straight-line
+// code: 11 FMAs of Horner, one exp2 on the special-function unit, no branch.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float za = fminf(fabsf(x) * 0.70710678118654752f, 4.f);
+  float p = -3.415930525e-06f;
+  p = fmaf(p, za, 8.719657761e-05f);
+  p = fmaf(p, za, -9.960989457e-04f);
+  p = fmaf(p, za, 6.759798689e-03f);
+  p = fmaf(p, za, -3.060881219e-02f);
+  p = fmaf(p, za, 9.900606157e-02f);
+  p = fmaf(p, za, -2.411291292e-01f);
+  p = fmaf(p, za, 4.644118264e-01f);
+  p = fmaf(p, za, -7.392278245e-01f);
+  p = fmaf(p, za, 9.974668638e-01f);
+  p = fmaf(p, za, -1.128182360e+00f);
+  p = fmaf(p, za, 9.999974348e-01f);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(za * (za * -1.4426950408889634f)));
+  const float h = 0.5f * p * e;
+  return x * (x >= 0.f ? 1.f - h : h);
+}
 
 // ---- epilogue ---------------------------------------------------------------
 // Eight warps: warp w reads TMEM lane quadrant w % 4 (32 accumulator rows, one
