@@ -313,29 +313,67 @@ def main():
     value = total / (ms_max / 1e3)
 
     # ---- end to end: pinned host inputs -> H2D -> forward -> D2H, every step ----
+    # A serving loop: the copies of step s+1's inputs and of step s's outputs
+    # run on a copy stream while the forward of step s runs (two device input
+    # and output sets). Every step's H2D and D2H is inside the timed region,
+    # which spans all K steps (one event pair around the loop, no L2 flush:
+    # each step's inputs arrive from the host and the forward's working set,
+    # ~1.3 GB at B=4096, is larger than L2).
     feats_h = host["feats"].half().pin_memory()
     nbr_h = torch.where(host["nbr"] >= npad, torch.full_like(host["nbr"], 0xFFFF), host["nbr"]).to(
         torch.int32).to(torch.uint16).pin_memory()
     mask_h = host["mask"].pin_memory()
     coords_h = host["coords"].to(torch.int16).pin_memory()
-    e2e_in = [torch.empty_like(x, device=device) for x in (feats_h, nbr_h, mask_h, coords_h)]
-    pol_h = torch.empty(shard, npad, dtype=torch.float32).pin_memory()
-    val_h = torch.empty(shard, 65, dtype=torch.float32).pin_memory()
+    host_in = (feats_h, nbr_h, mask_h, coords_h)
+    e2e_in = [[torch.empty_like(x, device=device) for x in host_in] for _ in range(2)]
+    e2e_out = [{"policy": torch.empty(shard, npad, dtype=torch.float32, device=device),
+                "value": torch.empty(shard, 65, dtype=torch.float32, device=device)} for _ in range(2)]
+    pol_h = [torch.empty(shard, npad, dtype=torch.float32).pin_memory() for _ in range(2)]
+    val_h = [torch.empty(shard, 65, dtype=torch.float32).pin_memory() for _ in range(2)]
+    main_st = torch.cuda.current_stream()
+    copy_st = torch.cuda.Stream()
 
-    def e2e_step():
-        for d, h in zip(e2e_in, (feats_h, nbr_h, mask_h, coords_h)):
-            d.copy_(h, non_blocking=True)
-        model.forward_policy_value(*e2e_in, out=out)
-        pol_h.copy_(out["policy"], non_blocking=True)
-        val_h.copy_(out["value"], non_blocking=True)
+    def e2e_run(k: int) -> float:
+        h2d_ev = [torch.cuda.Event() for _ in range(2)]
+        fwd_ev = [torch.cuda.Event() for _ in range(2)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(main_st)
+        copy_st.wait_stream(main_st)
 
-    e2e_times = time_steps(e2e_step, args.steps, args.warmup, flush)
-    t2 = torch.tensor([statistics.mean(e2e_times)], device=device, dtype=torch.float64)
+        def h2d(step: int):
+            b = step % 2
+            with torch.cuda.stream(copy_st):
+                if step >= 2:
+                    copy_st.wait_event(fwd_ev[b])  # the forward that last read buffer b
+                for d, h in zip(e2e_in[b], host_in):
+                    d.copy_(h, non_blocking=True)
+                h2d_ev[b].record(copy_st)
+
+        h2d(0)
+        for step in range(k):
+            b = step % 2
+            if step + 1 < k:
+                h2d(step + 1)
+            main_st.wait_event(h2d_ev[b])
+            model.forward_policy_value(*e2e_in[b], out=e2e_out[b])
+            fwd_ev[b].record(main_st)
+            with torch.cuda.stream(copy_st):
+                copy_st.wait_event(fwd_ev[b])
+                pol_h[b].copy_(e2e_out[b]["policy"], non_blocking=True)
+                val_h[b].copy_(e2e_out[b]["value"], non_blocking=True)
+        main_st.wait_stream(copy_st)
+        end.record(main_st)
+        end.synchronize()
+        return start.elapsed_time(end) / k
+
+    e2e_run(args.warmup)
+    torch.cuda.synchronize()
+    t2 = torch.tensor([e2e_run(args.steps)], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = total / (float(t2.item()) / 1e3)
-    h2d = sum(x.numel() * x.element_size() for x in (feats_h, nbr_h, mask_h, coords_h))
-    d2h = pol_h.numel() * 4 + val_h.numel() * 4
+    h2d = sum(x.numel() * x.element_size() for x in host_in)
+    d2h = pol_h[0].numel() * 4 + val_h[0].numel() * 4
 
     # ---- dominant kernel: the ConvBlock gather-GEMM at the bench shape ----
     roofline = None
@@ -390,7 +428,9 @@ def main():
             },
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "positions/s", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h)},
+                    "d2h_bytes_per_step": int(d2h),
+                    "note": "public module call per step; H2D of the next step and D2H of this step on a "
+                            "copy stream overlapping the forward; timed over all steps"},
             "gpu_launches": launches,
             "clocks": clocks,
         }
