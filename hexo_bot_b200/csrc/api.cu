@@ -360,9 +360,9 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
   const int tiles = (npos + ppt - 1) / ppt;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   if (heavy)
-    launch_ex(conv_ts_kernel<T, true>, grid, kConvThreads, smem, st, a, geo, mx, mw, m16, m32, stages);
+    launch_ex(conv_ts_kernel<T, true>, grid, conv_ts_threads(true), smem, st, a, geo, mx, mw, m16, m32, stages);
   else
-    launch_ex(conv_ts_kernel<T, false>, grid, kConvThreads, smem, st, a, geo, mx, mw, m16, m32, stages);
+    launch_ex(conv_ts_kernel<T, false>, grid, conv_ts_threads(false), smem, st, a, geo, mx, mw, m16, m32, stages);
   if (sync_debug())
     fprintf(stderr, "[sb] conv_ts M=%d C=%d ppt=%d win=%d stages=%d smem=%d grid=%d flags=%d\n", a.M, C, ppt,
             win_rows, stages, smem, grid, a.flags);

@@ -14,8 +14,9 @@
 // memory, so shared-memory bandwidth is spent on the weights and the gather
 // reads only. The epilogue is the eight-warp epilogue of gemm_ws_kernel.
 //
-// Warp roles (480 threads): 0-7 epilogue, 8 MMA issue, 9 weight producer,
-// 10-13 A builders, 14 window producer.
+// Warp roles (480 threads; 608 in the light instantiation): 0-7 epilogue,
+// 8 MMA issue, 9 weight producer, 10-13 A builders, 14 window producer,
+// 15-18 the second A-builder set (light instantiation only).
 #pragma once
 
 #include "gemm.cuh"
@@ -24,6 +25,11 @@ namespace sb {
 
 constexpr int kConvWarps = 15;
 constexpr int kConvThreads = kConvWarps * 32;
+// The light instantiation (no residual, no TMA epilogue) adds a second set of
+// four A-builder warps (warps 15-18): its registers fit 19 warps without
+// spilling, and the builders are on the per-stage critical path.
+constexpr int kConvBuilder1 = 15;
+__host__ __device__ constexpr int conv_ts_threads(bool heavy) { return heavy ? kConvThreads : kConvThreads + 128; }
 constexpr int kConvMmaWarp = 8;
 constexpr int kConvWProducer = 9;
 constexpr int kConvBuilder0 = 10;
@@ -59,11 +65,12 @@ __host__ __device__ constexpr int conv_ts_stages(int c, int win_rows, bool tma_e
 }
 
 template <typename T, bool HEAVY>
-__global__ void __launch_bounds__(kConvThreads, 1)
+__global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
     conv_ts_kernel(const GemmArgs a, const ConvTsGeom geo, const __grid_constant__ CUtensorMap tmap_x,
                    const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_o16,
                    const __grid_constant__ CUtensorMap tmap_o32, int stages) {
   extern __shared__ uint8_t smem_raw[];
+  constexpr int kSets = HEAVY ? 1 : 2;  // A-builder warp sets
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -114,12 +121,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar + 8 * s, 1 + 4);
+      mbar_init(full_bar + 8 * s, 1 + 4 * kSets);
       mbar_init(empty_bar + 8 * s, 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(winf_bar + 8 * i, 1);
-      mbar_init(wine_bar + 8 * i, 4);
+      mbar_init(wine_bar + 8 * i, 4 * kSets);
       mbar_init(accf_bar + 8 * i, 1);
       mbar_init(acce_bar + 8 * i, kEpiWarps);
     }
@@ -178,8 +185,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp >= kConvBuilder0 && warp < kConvBuilder0 + 4) {
+  } else if ((warp >= kConvBuilder0 && warp < kConvBuilder0 + 4) || warp >= kConvBuilder1) {
     // ------------------------------------------------------------ A builders
+    // kSets sets of four warps (one per TMEM lane quadrant in each set); with
+    // two sets, set bs builds chunk bs of every two-chunk stage
+    const int bs = warp >= kConvBuilder1 ? 1 : 0;
     const int quad = warp & 3;        // TMEM lanes [32 quad, 32 quad + 32)
     const int row = quad * 32 + lane; // row within the tile
     const uint32_t tlane = tmem_base + ((uint32_t)(quad * 32) << 16);
@@ -235,33 +245,61 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           v[4 * p + 3] = u.w & keep;
         }
       };
-      // Software pipeline: the gather of chunk c + 1 overlaps the TMEM store
-      // of chunk c; a stage (two chunks) is published once its stores have
-      // completed.
       uint32_t va[32], vb[32];
-      gather(0, va);
-      for (int q = 0; q < nst; ++q) {
-        const uint32_t ai = ac + q;
-        const int slot = ai % S;
-        const bool free_ok = mbar_wait(empty_bar + 8 * slot, ((ai / S) & 1) ^ 1);
-        ok = __all_sync(0xffffffffu, free_ok) != 0;
-        if (!ok) {
-          if (lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
-          break;
+      if constexpr (kSets == 1) {
+        // Software pipeline: the gather of chunk c + 1 overlaps the TMEM store
+        // of chunk c; a stage (two chunks) is published once its stores have
+        // completed.
+        gather(0, va);
+        for (int q = 0; q < nst; ++q) {
+          const uint32_t ai = ac + q;
+          const int slot = ai % S;
+          const bool free_ok = mbar_wait(empty_bar + 8 * slot, ((ai / S) & 1) ^ 1);
+          ok = __all_sync(0xffffffffu, free_ok) != 0;
+          if (!ok) {
+            if (lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
+            break;
+          }
+          tc_fence_after();
+          const int c0 = q * kConvStageChunks;
+          __syncwarp();
+          tmem_st32(tlane + a_col0 + slot * (32 * kConvStageChunks), va);
+          if (c0 + 1 < nk) gather(c0 + 1, vb);
+          __syncwarp();
+          if (c0 + 1 < nk) tmem_st32(tlane + a_col0 + slot * (32 * kConvStageChunks) + 32, vb);
+          if (c0 + 2 < nk) gather(c0 + 2, va);
+          __syncwarp();
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(full_bar + 8 * slot);
         }
-        tc_fence_after();
-        const int c0 = q * kConvStageChunks;
-        __syncwarp();
-        tmem_st32(tlane + a_col0 + slot * (32 * kConvStageChunks), va);
-        if (c0 + 1 < nk) gather(c0 + 1, vb);
-        __syncwarp();
-        if (c0 + 1 < nk) tmem_st32(tlane + a_col0 + slot * (32 * kConvStageChunks) + 32, vb);
-        if (c0 + 2 < nk) gather(c0 + 2, va);
-        __syncwarp();
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(full_bar + 8 * slot);
+      } else {
+        // Two sets: set bs stores chunk bs of each stage; the gather of its
+        // chunk of the next stage overlaps the store of the current one.
+        auto step = [&](int q, uint32_t (&cur)[32], uint32_t (&nxt)[32]) -> bool {
+          const uint32_t ai = ac + q;
+          const int slot = ai % S;
+          const bool free_ok = mbar_wait(empty_bar + 8 * slot, ((ai / S) & 1) ^ 1);
+          if (!__all_sync(0xffffffffu, free_ok)) return false;
+          tc_fence_after();
+          const int c = q * kConvStageChunks + bs;
+          __syncwarp();
+          if (c < nk) tmem_st32(tlane + a_col0 + slot * (32 * kConvStageChunks) + bs * 32, cur);
+          if (c + kConvStageChunks < nk) gather(c + kConvStageChunks, nxt);
+          __syncwarp();
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(full_bar + 8 * slot);
+          return true;
+        };
+        if (bs < nk) gather(bs, va);
+        for (int q = 0; q < nst && ok; q += 2) {
+          ok = step(q, va, vb);
+          if (ok && q + 1 < nst) ok = step(q + 1, vb, va);
+        }
+        if (!ok && lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
       }
       ac += nst;
       if (!ok) break;
