@@ -315,29 +315,38 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
 template <typename T>
 int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) {
   const int C = a.n_total;
+  // Input channels: C (64-column boxes), or a narrow 16 / 32 (the stem's
+  // feature planes: one box of cin columns, K chunks spanning several taps).
+  const bool narrow = a.cin == 16 || a.cin == 32;
   // TMEM: two C-column accumulators plus >= 2 A slots of 32 columns in 512.
-  if (a.taps != 7 || !a.gidx || a.cin != C || C % 64 || 2 * C + 64 > 512 || cells <= 0 || cells > kBlockM ||
-      xrows < cells)
+  if (a.taps != 7 || !a.gidx || (a.cin != C && !narrow) || C % 64 || 2 * C + 64 > 512 || cells <= 0 ||
+      cells > kBlockM || xrows < cells)
     return 1;
-  if (a.lda != C || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16 || producer_mode() == 1) return 1;
+  if (a.lda != a.cin || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16 || producer_mode() == 1) return 1;
   // positions per tile: 4, 2 or 1 (each position owns 128 / ppt TMEM lanes)
   int ppt = 4;
   while (ppt > 1 && (cells > kBlockM / ppt || ppt * xrows > 256)) ppt >>= 1;
   if (cells > kBlockM / ppt || ppt * xrows > 256) return 1;
   const int win_rows = ppt * xrows;
-  const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B)) != 0;
+  const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B | EPI_OUT32)) != 0;
   if (heavy && (a.flags & (EPI_RES16 | EPI_OUT32B | EPI_HEAD))) return 1;  // not in the TMA epilogue
   const int stages = conv_ts_stages(C, win_rows, heavy);
   const int smem = conv_ts_smem_bytes(C, stages, win_rows, heavy);
   if (smem > 227 * 1024) return 1;
   if (a.M <= 0 || npos <= 0) return SB_OK;
   a.bn = C;
-  a.kpad = 7 * C;
+  a.kpad = round_up(7 * a.cin, kChunkK);
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mx, mw;
   memset(&mx, 0, sizeof(mx));
   memset(&mw, 0, sizeof(mw));
-  if (int s = make_tmap(&mx, a.A, bf16, C, (long long)npos * xrows, C, win_rows)) return s;
+  if (narrow) {
+    if (int s = make_tmap_ex(&mx, a.A, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                             a.cin, (long long)npos * xrows, a.cin, a.cin, win_rows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return s;
+  } else if (int s = make_tmap(&mx, a.A, bf16, C, (long long)npos * xrows, C, win_rows)) {
+    return s;
+  }
   if (int s = make_tmap(&mw, a.Bw, bf16, a.kpad, C, a.kpad, C)) return s;
   // heavy epilogue: TMA stores / residual loads through 3D maps (columns,
   // rows of a position's block, positions): rows past a block are clipped
@@ -639,7 +648,7 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
       g.flags |= EPI_LN_B;
       g.ln_b_w = net->attn[0].ln1_w; g.ln_b_b = net->attn[0].ln1_b;
     }
-    if (int s = launch_gemm<__half>(g, st)) return s;
+    if (int s = launch_conv<__half>(g, B, npad, S, st)) return s;
   }
 
   int ci = 0, ai = 0;

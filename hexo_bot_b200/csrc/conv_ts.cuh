@@ -76,7 +76,13 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
   const int lane = tid & 31;
   const int S = stages;
   const int C = a.n_total;  // == a.bn == a.cin
-  const int nbox = C / 64;
+  // Window: C / 64 boxes of 64 columns (128-byte swizzled rows) when the input
+  // has C channels; one unswizzled box of cin columns for a narrow input (the
+  // stem's 16 feature planes), whose K chunks then span several taps.
+  const int cin = a.cin;
+  const bool narrow = cin < 64;
+  const int nbox = narrow ? 1 : C / 64;
+  const int win_row_bytes = narrow ? cin * 2 : 128;  // bytes of one window row in one box
   const int win_rows = geo.ppt * geo.xrows;
   const int box_bytes = conv_win_box_bytes(win_rows);
   const int lpb = kBlockM / geo.ppt;  // TMEM lanes per position
@@ -87,7 +93,7 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
   const uint32_t chunk_bytes = C * 128;                 // one 64-wide K chunk of the weights
   const uint32_t stage_bytes = kConvStageChunks * chunk_bytes;
   const uint32_t win_off = S * stage_bytes;                             // [2][nbox][box_bytes]
-  const uint32_t epi_off = win_off + 2 * nbox * box_bytes;
+  const uint32_t epi_off = win_off + 2 * (C / 64) * box_bytes;          // as sized by conv_ts_smem_bytes
   float* vecs = reinterpret_cast<float*>(gbase + epi_off);
   float4* xch_all = reinterpret_cast<float4*>(gbase + epi_off + kEpiVecFloats * 4);
   // TMA epilogue staging (heavy instantiation), 1024-aligned
@@ -156,7 +162,7 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
           if (a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
         }
         if (!ok) break;
-        mbar_arrive_expect_tx(winf_bar + 8 * wb, nbox * win_rows * 128);
+        mbar_arrive_expect_tx(winf_bar + 8 * wb, nbox * win_rows * win_row_bytes);
         const int row0 = t * geo.ppt * geo.xrows;
         for (int bx = 0; bx < nbox; ++bx)
           tma_load_2d(base + win_off + (wb * nbox + bx) * box_bytes, &tmap_x, bx * 64, row0, winf_bar + 8 * wb);
@@ -227,6 +233,27 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
       // missing tap) into 32 registers
       auto gather = [&](int c, uint32_t (&v)[32]) {
         const int k0 = c * kChunkK;
+        if (narrow) {
+          // 8 pieces of 8 channels; piece p is channel (k0 + 8p) % cin of tap
+          // (k0 + 8p) / cin (taps past the seventh are the K padding: zeros)
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            const int kk = k0 + 8 * p;
+            const int tap = kk / cin;
+            int r = src[0];
+#pragma unroll
+            for (int k = 1; k < 7; ++k) r = tap == k ? src[k] : r;
+            r = tap < 7 ? r : -1;
+            const int rr = r < 0 ? 0 : r;
+            const uint32_t keep = r < 0 ? 0u : 0xffffffffu;
+            const uint4 u = lds128(win + rr * win_row_bytes + (kk - tap * cin) * 2);
+            v[4 * p] = u.x & keep;
+            v[4 * p + 1] = u.y & keep;
+            v[4 * p + 2] = u.z & keep;
+            v[4 * p + 3] = u.w & keep;
+          }
+          return;
+        }
         const int tap = k0 / C;
         const int bx = (k0 - tap * C) >> 6;
         int r = src[0];
