@@ -489,7 +489,7 @@ int launch_attention(AttnArgs a, cudaStream_t st) {
 constexpr size_t kGidxSlack = 64;
 
 struct FwdLayout {
-  size_t seq32, lnf32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, total;
+  size_t seq32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, total;
 };
 
 FwdLayout fwd_layout(int C, int B, int npad) {
@@ -504,7 +504,6 @@ FwdLayout fwd_layout(int C, int B, int npad) {
     return o;
   };
   L.seq32 = take(R * C * 4);
-  L.lnf32 = take(R * C * 4);
   L.xa16 = take(R * C * 2);
   L.y16 = take(R * C * 2);
   L.qkv16 = take(R * 3 * C * 2);
@@ -570,7 +569,6 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   float* seq32 = reinterpret_cast<float*>(ws + L.seq32);
-  float* lnf32 = reinterpret_cast<float*>(ws + L.lnf32);
   __half* xa16 = reinterpret_cast<__half*>(ws + L.xa16);
   __half* y16 = reinterpret_cast<__half*>(ws + L.y16);
   __half* qkv16 = reinterpret_cast<__half*>(ws + L.qkv16);
@@ -702,8 +700,7 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
       gf2.flags = EPI_MASK | EPI_RESID | EPI_OUT32 | EPI_OUT16 | EPI_LN_B;
       gf2.gamma = w.gamma_mlp; gf2.out32 = seq32; gf2.ld32 = C; gf2.out16 = xa16; gf2.ld16 = C;
       if (pos == nb - 1) {
-        gf2.ln_b_w = net->ln_final_w; gf2.ln_b_b = net->ln_final_b;
-        gf2.flags |= EPI_OUT32B; gf2.out32b = lnf32; gf2.ld32b = C;
+        gf2.ln_b_w = net->ln_final_w; gf2.ln_b_b = net->ln_final_b;  // xa16 = ln_final(stream), every row
       } else {
         const int na = ai + 1;
         gf2.ln_b_w = net->attn[na].ln1_w; gf2.ln_b_b = net->attn[na].ln1_b;
@@ -723,7 +720,7 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
   // value (+ moves-left) heads and decode (model.py:984-1003, losses.py:40-61)
   {
     HeadsArgs h{};
-    h.lnf32 = lnf32; h.rowmask = rowmask; h.B = B; h.S = S; h.C = C;
+    h.lnf16 = xa16; h.rowmask = rowmask; h.B = B; h.S = S; h.C = C;
     h.vr_wT = net->value_red_wT; h.vr_b = net->value_red_b; h.vh_wT = net->value_head_wT; h.vh_b = net->value_head_b;
     h.value_logits = out->value_logits; h.value = out->value;
     if (out->ml_logits) {

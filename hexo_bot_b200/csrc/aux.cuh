@@ -197,7 +197,7 @@ __global__ void pair_u8_kernel(const void* coords, int cdtype, const void* mask,
 }
 
 struct HeadsArgs {
-  const float* lnf32;     // (B*S, C): ln_final output, token + cell rows
+  const __half* lnf16;    // (B*S, C): ln_final output (f16, the policy conv's input too), token + cell rows
   const float* rowmask;   // (B*S)
   int B, S, C;
   const float* vr_wT; const float* vr_b; const float* vh_wT; const float* vh_b;
@@ -278,7 +278,7 @@ __device__ void heads_pass(const HeadsArgs& a, int pass, float* sm, int b0, int 
   for (int idx = tid; idx < P * 2 * C; idx += kHeadsThreads) {
     const int c = idx / P, p = idx - c * P;  // consecutive threads: consecutive positions of one channel
     float v = 0.f;
-    if (p < npos) v = __ldg(a.lnf32 + ((long long)(b0 + p) * S + ta + (c >= C ? 1 : 0)) * C + (c % C));
+    if (p < npos) v = __half2float(a.lnf16[((long long)(b0 + p) * S + ta + (c >= C ? 1 : 0)) * C + (c % C)]);
     vin[idx] = v;
   }
   if (pass == 0) {  // the cell mean is shared by both heads (kept in vin[2C, 3C))
@@ -294,22 +294,23 @@ __device__ void heads_pass(const HeadsArgs& a, int pass, float* sm, int b0, int 
         float cnt = 0.f;
         if (live) {
           for (int n0 = part; n0 < npad; n0 += 32) {
-            float4 v[16];
+            uint2 v[16];  // four f16 channels
             float mk[16];
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
               const int n = n0 + 2 * q;
               const bool in = n < npad;
               mk[q] = in ? __ldg(a.rowmask + base + n) : 0.f;
-              v[q] = in ? __ldg(reinterpret_cast<const float4*>(a.lnf32 + (base + n) * C) + c4)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
+              v[q] = in ? __ldg(reinterpret_cast<const uint2*>(a.lnf16 + (base + n) * C) + c4) : make_uint2(0u, 0u);
             }
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
-              s.x = fmaf(v[q].x, mk[q], s.x);
-              s.y = fmaf(v[q].y, mk[q], s.y);
-              s.z = fmaf(v[q].z, mk[q], s.z);
-              s.w = fmaf(v[q].w, mk[q], s.w);
+              const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v[q].x));
+              const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v[q].y));
+              s.x = fmaf(lo.x, mk[q], s.x);
+              s.y = fmaf(lo.y, mk[q], s.y);
+              s.z = fmaf(hi.x, mk[q], s.z);
+              s.w = fmaf(hi.y, mk[q], s.w);
               cnt += mk[q];
             }
           }
