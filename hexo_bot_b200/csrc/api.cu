@@ -328,7 +328,9 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
   while (ppt > 1 && (cells > kBlockM / ppt || ppt * xrows > 256)) ppt >>= 1;
   if (cells > kBlockM / ppt || ppt * xrows > 256) return 1;
   const int win_rows = ppt * xrows;
-  const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B | EPI_OUT32)) != 0;
+  // rows written by TMA (fp32 and 16-bit outputs, residual loads) use the TMA
+  // epilogue; the light instantiation (per-row stores) remains for the policy head
+  const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B | EPI_OUT32 | EPI_OUT16)) != 0;
   if (heavy && (a.flags & (EPI_RES16 | EPI_OUT32B | EPI_HEAD))) return 1;  // not in the TMA epilogue
   const int stages = conv_ts_stages(C, win_rows, heavy);
   const int smem = conv_ts_smem_bytes(C, stages, win_rows, heavy);

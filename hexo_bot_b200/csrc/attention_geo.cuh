@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
         }
       }
       // normalise by the row sums and store (canonical rows >= S are padding)
-      const float i0 = 1.f / os[0], i1 = 1.f / os[2];
+      const float i0 = __fdividef(1.f, os[0]), i1 = __fdividef(1.f, os[2]);  // row sums are >= 1
       const int r0 = qt * 16 + g, r1 = r0 + 8;
       T* oh = Ob + (long long)h * a.out_head_stride + 2 * t4;
       if (r0 < S) {
