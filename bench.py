@@ -45,7 +45,7 @@ METRIC = "Shrimp positions/sec at batch 4096 (1/2/4/8 B200); p50 latency at batc
 LATENCY_BATCHES = (1, 16, 64, 256, 1024)
 # dram bytes (read + write) of one dominant-kernel launch at the bench shape,
 # from the committed ncu capture (profiles/conv_ts_main.md); None until captured.
-DOMINANT_TRAFFIC_BYTES = 88_497_152
+DOMINANT_TRAFFIC_BYTES = 94_057_984
 
 
 def load_peaks() -> dict:
