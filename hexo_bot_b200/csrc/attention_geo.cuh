@@ -286,6 +286,17 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
     }
     const uint32_t sbuf = base + buf * L.buf_bytes;
     T* Ob = reinterpret_cast<T*>(a.out) + (long long)b * a.out_pos_stride;
+    // This lane's K and V row of every 16-key block (canonical order), as the
+    // row's byte offset with its swizzle phase in bits 4-6: the ldmatrix address
+    // of chunk c is then box + (ro ^ (c << 4)) (see geo_swz).
+    uint32_t kro[(NJ + 1) / 2], vro[(NJ + 1) / 2];
+#pragma unroll
+    for (int j2 = 0; j2 < (NJ + 1) / 2; ++j2) {
+      const int rk = rowof[j2 * 16 + (lane & 7) + ((lane >> 4) << 3)];
+      const int rv = rowof[j2 * 16 + (lane & 7) + (((lane >> 3) & 1) << 3)];
+      kro[j2] = rk * 128 + ((rk & 7) << 4);
+      vro[j2] = rv * 128 + ((rv & 7) << 4);
+    }
 
     for (int task = warp; task < H * QT; task += kGeoWarps) {
       const int h = task / QT, qt = task - h * QT;
@@ -305,7 +316,7 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
       for (int jp = 0; jp < (NJ + 1) / 2; ++jp) {
         {
           uint32_t kb[4];
-          ldmatrix_x4(kb, geo_swz(sK, rowof[jp * 16 + (lane & 7) + ((lane >> 4) << 3)], cq + ((lane >> 3) & 1)));
+          ldmatrix_x4(kb, sK + (kro[jp] ^ ((uint32_t)(cq + ((lane >> 3) & 1)) << 4)));
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int jt = 2 * jp + u;
@@ -344,16 +355,19 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int jt = 2 * kk + u;
-            const float p0 = ex2_approx(fmaf(s[jt][0], c2, n0));
-            const float p1 = ex2_approx(fmaf(s[jt][1], c2, n0));
-            const float p2 = ex2_approx(fmaf(s[jt][2], c2, n1));
-            const float p3 = ex2_approx(fmaf(s[jt][3], c2, n1));
-            pa[2 * u] = MmaTraits<T>::pack(p0, p1);
-            pa[2 * u + 1] = MmaTraits<T>::pack(p2, p3);
+            if (jt < NJ) {
+              const float p0 = ex2_approx(fmaf(s[jt][0], c2, n0));
+              const float p1 = ex2_approx(fmaf(s[jt][1], c2, n0));
+              const float p2 = ex2_approx(fmaf(s[jt][2], c2, n1));
+              const float p3 = ex2_approx(fmaf(s[jt][3], c2, n1));
+              pa[2 * u] = MmaTraits<T>::pack(p0, p1);
+              pa[2 * u + 1] = MmaTraits<T>::pack(p2, p3);
+            } else {
+              pa[2 * u] = pa[2 * u + 1] = 0u;  // the key tile past S (odd NJ)
+            }
           }
           uint32_t vb[4];
-          ldmatrix_x4_trans(vb,
-                            geo_swz(sV, rowof[kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3)], cq + (lane >> 4)));
+          ldmatrix_x4_trans(vb, sV + (vro[kk] ^ ((uint32_t)(cq + (lane >> 4)) << 4)));
           geo_mma<T>(o0, pa, vb[0], vb[1]);
           geo_mma<T>(o1, pa, vb[2], vb[3]);
           geo_mma<T>(os, pa, one2, one2);

@@ -157,6 +157,41 @@ def test_full_size_properties_main():
     assert torch.equal(again["policy"], full["policy"]) and torch.equal(again["value"], full["value"])
 
 
+def permute_cells(batch, seed):
+    """The same positions with each position's cells in a random order: features,
+    mask and coordinates permuted, neighbour indices remapped (missing stays Npad)."""
+
+    g = torch.Generator().manual_seed(seed)
+    out = {k: v.clone() for k, v in batch.items()}
+    B, N = batch["mask"].shape
+    perms = []
+    for i in range(B):
+        perm = torch.randperm(N, generator=g)
+        inv = torch.empty_like(perm)
+        inv[perm] = torch.arange(N)
+        out["feats"][i] = batch["feats"][i][perm]
+        out["mask"][i] = batch["mask"][i][perm]
+        out["coords"][i] = batch["coords"][i][perm]
+        nb = batch["nbr"][i][perm]
+        out["nbr"][i] = torch.where(nb < N, inv[nb.clamp(max=N - 1)], nb)
+        perms.append(perm)
+    return out, torch.stack(perms)
+
+
+def test_forward_is_equivariant_under_cell_order():
+    """Cells in another order give the same per-cell policy logits and the same
+    value: the geometry-cached attention maps every position onto one canonical
+    cell order, so its cache must not depend on the order the rows arrive in."""
+    model, _ = build(MAIN, 4, True)
+    batch = P.disk_batch(96, 5, 60, 4)
+    shuffled, perms = permute_cells(batch, 11)
+    a = run(model, batch)
+    b = run(model, shuffled)
+    gathered = torch.gather(a["policy"], 1, perms)
+    assert (b["policy"] - gathered).abs().max().item() <= 1e-4
+    assert (O.decode_binned_value(b["value"]) - O.decode_binned_value(a["value"])).abs().max().item() <= 1e-4
+
+
 def test_weights_repack_after_update():
     batch = P.disk_batch(4, 0, 30, 4)
     model, _ = build(SMOKE, 0, False)
