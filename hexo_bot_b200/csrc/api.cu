@@ -408,7 +408,7 @@ int launch_attention(AttnArgs a, cudaStream_t st) {
       a.S <= kGeoMaxS && 2 * (a.S - a.ntok) + a.S <= kGeoThreads && a.table_rows <= 255 && a.coords && a.lut) {
     const long long C = (long long)a.H * a.D;
     const T* q = reinterpret_cast<const T*>(a.q);
-    const AttnGeoLayout L = attn_geo_layout(a.S, a.H);
+    const AttnGeoLayout L = attn_geo_layout(a.S);
     if (a.k == q + C && a.v == q + 2 * C && a.row_stride == 3 * C && a.head_stride == a.D &&
         a.pos_stride == (long long)a.S * 3 * C && (uintptr_t)a.q % 16 == 0 && L.total <= 227 * 1024 &&
         L.nj >= 8 && L.nj <= 10) {
@@ -418,7 +418,11 @@ int launch_attention(AttnArgs a, cudaStream_t st) {
       if (int s = make_tmap(&tm, a.q, std::is_same<T, __nv_bfloat16>::value, 3 * C, (long long)a.B * a.S, 3 * C,
                             a.S))
         return s;
-      const int grid = a.B < num_sms() ? a.B : num_sms();
+      // two CTAs per SM, each on one group of four heads; a group's CTAs
+      // stride over the positions
+      const int groups = a.H / kGeoHeads;
+      const int per_group = a.B < 2 * num_sms() / groups ? a.B : 2 * num_sms() / groups;
+      const int grid = groups * (per_group > 0 ? per_group : 1);
 #define SB_GEO_CASE(NJV)                                                                              \
   case NJV:                                                                                           \
     if (int s = ensure_smem(reinterpret_cast<const void*>(attn_geo_kernel<T, NJV>), L.total)) return s; \

@@ -12,7 +12,7 @@
 // regime every position of a batch covers the same set of cells, only in a
 // different row order (the support lists legal cells first, then stones, then
 // the rest). Attention is equivariant under a permutation of the rows, so each
-// CTA keeps the whole bias tensor of the last cell set it saw in shared memory
+// CTA keeps the bias tensor of its heads for the last cell set it saw in shared memory
 // ([head][query][key] in f16, pre-divided by the softmax scale, in that set's
 // canonical row order: the cells sorted by coordinates) and, per position,
 // only maps its rows onto the canonical order: a 35x35 coordinate window
@@ -23,7 +23,8 @@
 // MMA as its C operand, which removes the per-score row-table and bias-table
 // lookups of the general kernel.
 //
-// Per CTA (one per SM, persistent over positions b = blockIdx.x, +gridDim.x, ...):
+// Per CTA (two per SM, each owning one group of four heads, persistent over
+// the positions: b = blockIdx.x / G, + gridDim.x / G, ... for G head groups):
 //   * q, k and v of a position arrive by TMA as 64-column boxes of S rows
 //     (128-byte swizzle), double buffered, so the next position streams in
 //     while this one is computed;
@@ -40,7 +41,8 @@
 namespace sb {
 
 constexpr int kGeoD = 16;          // head_dim of this kernel
-constexpr int kGeoWarps = 20;      // two (head, query-tile) tasks per warp at H = 8, S = 69
+constexpr int kGeoHeads = 4;       // heads per CTA: one 64-column box of q, k and v
+constexpr int kGeoWarps = 10;      // two (head, query-tile) tasks per warp at S = 69
 constexpr int kGeoThreads = kGeoWarps * 32;
 constexpr int kGeoMaxS = 80;
 
@@ -50,10 +52,10 @@ struct AttnGeoLayout {
   int nj;         // 8-key tiles covering S
   int nk;         // nj * 8: keys per cached bias row
   int box_bytes;  // one 64-column box of sp rows
-  int nbox;       // boxes of one position (q, k and v)
+  int nbox;       // boxes of one position (q, k and v of the CTA's head group)
   int buf_bytes;  // one position
-  int cache_off;  // f16 bias [H][S][nk]
-  int table_off;  // f32 bias table [256][H] (row 255 = excluded key)
+  int cache_off;  // f16 bias [kGeoHeads][S][nk]
+  int table_off;  // f32 bias table [256][kGeoHeads] (row 255 = excluded key)
   int lut_off;    // u8 35x35 clamped-offset LUT
   int geo_off;    // canonical cell coordinates [2][80] i32, key liveness [80] f32,
                   // coordinate window [35*35] u8, canonical index -> row [80] u8,
@@ -62,17 +64,17 @@ struct AttnGeoLayout {
   int total;      // including the slack that aligns the dynamic base
 };
 
-__host__ __device__ inline AttnGeoLayout attn_geo_layout(int S, int H) {
+__host__ __device__ inline AttnGeoLayout attn_geo_layout(int S) {
   AttnGeoLayout L{};
   L.sp = attn_pad16(S);
   L.nj = (S + 7) / 8;
   L.nk = L.nj * 8;
   L.box_bytes = L.sp * 128;
-  L.nbox = 3 * H * kGeoD / 64;
+  L.nbox = 3;
   L.buf_bytes = L.nbox * L.box_bytes;
   L.cache_off = 2 * L.buf_bytes;
-  L.table_off = L.cache_off + attn_round16(H * S * L.nk * 2);
-  L.lut_off = L.table_off + 256 * H * 4;
+  L.table_off = L.cache_off + attn_round16(kGeoHeads * S * L.nk * 2);
+  L.lut_off = L.table_off + 256 * kGeoHeads * 4;
   L.geo_off = L.lut_off + attn_round16(kLutW * kLutW);
   L.bar_off = L.geo_off + 2 * kGeoMaxS * 4 + kGeoMaxS * 4 + attn_round16(kLutW * kLutW) + kGeoMaxS +
               2 * kGeoMaxS * 4;
@@ -116,7 +118,7 @@ __device__ __forceinline__ uint32_t geo_swz(uint32_t box, int r, int c) {
 // NJ = ceil(S / 8) is a template parameter so the score, softmax and P.V
 // loops unroll completely without tail branches.
 template <typename T, int NJ>
-__global__ void __launch_bounds__(kGeoThreads, 1)
+__global__ void __launch_bounds__(kGeoThreads, 2)
     attn_geo_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmap) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -125,9 +127,13 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int S = a.S, H = a.H, ntok = a.ntok, ncell = S - ntok;
-  const AttnGeoLayout L = attn_geo_layout(S, H);
+  const AttnGeoLayout L = attn_geo_layout(S);
   const int QT = L.sp / 16, NK = L.nk;  // NK == 8 * NJ
-  const int nbh = H / 4;  // 64-column boxes per tensor (four heads of 16 columns each)
+  // head group of this CTA (four heads = one 64-column box of each of q, k, v);
+  // the CTAs of a group stride over the positions
+  const int G = H / kGeoHeads;
+  const int gi = blockIdx.x % G;
+  const int b0 = blockIdx.x / G, pstride = gridDim.x / G;
   __half* cache = reinterpret_cast<__half*>(gb + L.cache_off);
   float* table_s = reinterpret_cast<float*>(gb + L.table_off);
   uint8_t* lut_s = gb + L.lut_off;
@@ -143,9 +149,10 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
   // rows of every box, barriers --------------------------------------------
   pdl_launch_dependents();
   const float inv_scale = sqrtf((float)a.D);
-  for (int i = tid; i < 256 * H; i += kGeoThreads) {
-    const int r = i / H, h = i - r * H;
-    table_s[i] = r < a.table_rows ? __ldg(a.table + (long long)r * H + h) * inv_scale : -INFINITY;
+  for (int i = tid; i < 256 * kGeoHeads; i += kGeoThreads) {
+    const int r = i / kGeoHeads, hl = i - r * kGeoHeads;
+    table_s[i] =
+        r < a.table_rows ? __ldg(a.table + (long long)r * H + gi * kGeoHeads + hl) * inv_scale : -INFINITY;
   }
   for (int i = tid; i < kLutW * kLutW; i += kGeoThreads) lut_s[i] = __ldg(a.lut + i);
   {
@@ -168,7 +175,9 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
     const uint32_t bar = full0 + 8 * buf;
     mbar_arrive_expect_tx(bar, (uint32_t)(L.nbox * S * 128));
     const uint32_t dst = base + buf * L.buf_bytes;
-    for (int x = 0; x < L.nbox; ++x) tma_load_2d(dst + x * L.box_bytes, &tmap, x * 64, b * S, bar);
+    // q, k, v boxes of the group's heads: columns x * C + gi * 64
+    for (int x = 0; x < L.nbox; ++x)
+      tma_load_2d(dst + x * L.box_bytes, &tmap, x * H * kGeoD + gi * 64, b * S, bar);
   };
   // this thread's cell (row ntok + tid) of position b: coordinates, liveness
   struct GeoCell {
@@ -204,26 +213,27 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
           row = lut_s[(dq + kLutM) * kLutW + dr + kLutM];
         }
       }
-      const float* tr = table_s + row * H;
+      const float* tr = table_s + row * kGeoHeads;
       __half* dst = cache + (long long)q * NK + k;
-      for (int h = 0; h < H; ++h) dst[(long long)h * S * NK] = __float2half_rn(tr[h]);
+#pragma unroll
+      for (int hl = 0; hl < kGeoHeads; ++hl) dst[(long long)hl * S * NK] = __float2half_rn(tr[hl]);
     }
   };
 
   if (tid == 0) {
-    if ((int)blockIdx.x < a.B) issue(blockIdx.x, 0);
-    if ((int)(blockIdx.x + gridDim.x) < a.B) issue(blockIdx.x + gridDim.x, 1);
+    if (b0 < a.B) issue(b0, 0);
+    if (b0 + pstride < a.B) issue(b0 + pstride, 1);
   }
   bool have = false;
   bool ok = true;
   int oq = 0, orr = 0;  // window origin: canonical cell 0
-  GeoCell nxt = load_cell((int)blockIdx.x < a.B ? blockIdx.x : 0);
+  GeoCell nxt = load_cell(b0 < a.B ? b0 : 0);
   const float c2 = a.scale_log2;  // scores here are Q.K + bias * sqrt(d); exp2 argument = (s - m) * c2
   const uint32_t one2 = geo_one2<T>();
   int j = 0;
-  for (int b = blockIdx.x; b < a.B; b += gridDim.x, ++j) {
+  for (int b = b0; b < a.B; b += pstride, ++j) {
     const GeoCell cur = nxt;
-    if (b + (int)gridDim.x < a.B) nxt = load_cell(b + gridDim.x);  // in flight during this position
+    if (b + pstride < a.B) nxt = load_cell(b + pstride);  // in flight during this position
     // map this position's cells onto the cached canonical order
     bool miss = !have;
     int canon = -1;
@@ -298,18 +308,19 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
       vro[j2] = rv * 128 + ((rv & 7) << 4);
     }
 
-    for (int task = warp; task < H * QT; task += kGeoWarps) {
-      const int h = task / QT, qt = task - h * QT;
-      const int cq = (h & 3) * 2;  // first 16-byte chunk of head h inside its box
-      const uint32_t sQ = sbuf + (h >> 2) * L.box_bytes;
-      const uint32_t sK = sQ + nbh * L.box_bytes;
-      const uint32_t sV = sK + nbh * L.box_bytes;
+    for (int task = warp; task < kGeoHeads * QT; task += kGeoWarps) {
+      const int hl = task / QT, qt = task - hl * QT;
+      const int h = gi * kGeoHeads + hl;  // head index in the layer
+      const int cq = hl * 2;              // first 16-byte chunk of the head inside its box
+      const uint32_t sQ = sbuf;
+      const uint32_t sK = sQ + L.box_bytes;
+      const uint32_t sV = sK + L.box_bytes;
       uint32_t qa[4];
       ldmatrix_x4(qa, geo_swz(sQ, rowof[qt * 16 + (lane & 15)], cq + (lane >> 4)));
       // this thread's two query rows of the cached bias (padding queries read row S-1)
       const int q0 = min(qt * 16 + g, S - 1), q1 = min(qt * 16 + g + 8, S - 1);
-      const __half2* bb0 = reinterpret_cast<const __half2*>(cache + ((long long)h * S + q0) * NK + 2 * t4);
-      const __half2* bb1 = reinterpret_cast<const __half2*>(cache + ((long long)h * S + q1) * NK + 2 * t4);
+      const __half2* bb0 = reinterpret_cast<const __half2*>(cache + ((long long)hl * S + q0) * NK + 2 * t4);
+      const __half2* bb1 = reinterpret_cast<const __half2*>(cache + ((long long)hl * S + q1) * NK + 2 * t4);
 
       float s[NJ + 1][4];
 #pragma unroll
@@ -389,14 +400,14 @@ __global__ void __launch_bounds__(kGeoThreads, 1)
       }
     }
     __syncthreads();  // every warp is done with buffer `buf`
-    if (tid == 0 && b + 2 * (int)gridDim.x < a.B) issue(b + 2 * gridDim.x, buf);
+    if (tid == 0 && b + 2 * pstride < a.B) issue(b + 2 * pstride, buf);
   }
   if (!ok) {
     // a TMA wait gave up: report it, then give the copies still in flight one
     // more bounded wait so none lands in shared memory after the CTA exits
     if (tid == 0) {
       if (a.err) atomicOr(a.err, SB_DEV_ERR_TIMEOUT);
-      const int b_last = blockIdx.x + (j + 1) * gridDim.x;
+      const int b_last = b0 + (j + 1) * pstride;
       mbar_wait(full0 + 8 * (j & 1), (j >> 1) & 1);
       if (b_last < a.B) mbar_wait(full0 + 8 * ((j + 1) & 1), ((j + 1) >> 1) & 1);
     }
