@@ -219,7 +219,8 @@ def run_reference(args, cfg):
         "metric": METRIC, "value": round(value, 2), "unit": "positions/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: seeded uniform-random legal play on the radius-4 disk",
+        "data": f"synthetic: seeded uniform-random legal play on the radius-{cfg['disk']} disk, "
+                f"0-{cfg['plies']} plies, random-init weights (seed {cfg['seed']})",
         "config": {"workload": f"{args.config} forward_policy_value (CPU reference restatement)",
                    "global_batch": cfg["batch"], "sample_per_step": sample},
         "impl": "reference",
