@@ -1,17 +1,23 @@
 """Benchmark: Shrimp-main forward_policy_value, positions/s at global batch 4096.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference] [--config main|stress|...]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference] [--config NAME]
+
+Configs: main (default), stress (config 5), smoke (config 1),
+and the two kernel microbenches attn_micro (config 2, sb_offset_attention) and
+conv19_micro (config 3, sb_raytap_conv).
 
 One process per GPU (torchrun for N > 1, NCCL). The global batch is split by
-position across ranks (strong scaling: 4096 positions in total); weights are
+position across ranks (strong scaling: the config's batch in total); weights are
 built on rank 0 and broadcast once over NCCL; there is no collective in the
-timed steps. Each timed step is one full forward over the rank's shard with its
-inputs resident in HBM; L2 is flushed between steps (outside the timed
-window). Step times are CUDA events on the launching stream; the reported time
-is the max over ranks. Rank 0 prints one JSON line.
+timed steps. Each timed step is one full forward (or one kernel call) over the
+rank's shard with its inputs resident in HBM; L2 is flushed between steps
+(outside the timed window). Step times are CUDA events on the launching
+stream; the reported time is the max over ranks. Rank 0 prints one JSON line.
 
-`--impl reference` times the CPU restatement of the reference forward on the
-host cores instead (the reference is Python/PyTorch; no GPU is used).
+`--impl reference` times the CPU restatement of the reference path (the oracle
+port, fp32 torch on the host cores) on a bounded sample of the same workload;
+the native line's `cpu_baseline` is that same measurement, run in a child
+process with the same arguments.
 """
 
 from __future__ import annotations
@@ -33,19 +39,30 @@ sys.path.insert(0, str(ROOT))
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
-CONFIGS = {
+from hexo_bot_b200 import microbench  # noqa: E402
+from hexo_bot_b200.microbench import disk_cells  # noqa: E402
+
+FORWARD_CONFIGS = {
     "main": dict(channels=128, attention_heads=8, trunk_layout="CCACCACCACCA", seed=0, disk=4, plies=60,
-                 batch=4096, mflop=321.7),
+                 batch=4096, mflop=321.7, cpu_sample=256),
     "stress": dict(channels=192, attention_heads=12, trunk_layout="CCACCACCACCA", seed=1, disk=8, plies=120,
-                   batch=1024, mflop=2599.3),
+                   batch=1024, mflop=2599.3, cpu_sample=32),
     "smoke": dict(channels=32, attention_heads=4, trunk_layout="CCA", seed=0, disk=4, plies=30, batch=64,
-                  mflop=6.5),
+                  mflop=6.5, cpu_sample=64),
 }
+MICRO_CONFIGS = {
+    "attn_micro": dict(**microbench.ATTN_MICRO, cpu_sample=512),
+    "conv19_micro": dict(**microbench.CONV19_MICRO, cpu_sample=256),
+}
+CONFIGS = {**FORWARD_CONFIGS, **MICRO_CONFIGS}
 METRIC = "Shrimp positions/sec at batch 4096 (1/2/4/8 B200); p50 latency at batch 256"
 LATENCY_BATCHES = (1, 16, 64, 256, 1024)
-# dram bytes (read + write) of one dominant-kernel launch at the bench shape,
-# from the committed ncu capture (profiles/conv_ts_main.md); None until captured.
-DOMINANT_TRAFFIC_BYTES = 94_057_984
+# DRAM bytes (read + write) of one launch of the dominant kernel, from an ncu
+# capture of that launch at the named (config, per-GPU batch); shapes that were
+# not captured report null.
+DOMINANT_TRAFFIC_BYTES: dict[tuple[str, int], int] = {
+    ("main", 4096): 94_057_984,
+}
 
 
 def load_peaks() -> dict:
@@ -116,23 +133,145 @@ class ClockSampler:
         }
 
 
+# ---- inputs -----------------------------------------------------------------------
+
+
 def make_batch(cfg: dict, count: int, start: int):
     from hexo_bot_b200 import positions
 
     return positions.disk_batch(count, cfg["seed"], cfg["plies"], cfg["disk"], start=start)
 
 
-def build_model(cfg: dict, device, rank: int, world: int):
-    from hexo_bot_b200.model import ShrimpNet
-    from hexo_bot_b200.sharding import broadcast_weights
+def micro_inputs(name: str, cfg: dict, count: int, start: int) -> dict:
+    from hexo_bot_b200 import microbench
 
-    kw = {k: cfg[k] for k in ("channels", "attention_heads", "trunk_layout")}
-    torch.manual_seed(cfg["seed"])
-    model = ShrimpNet(**kw).to(device)
-    if world > 1:
-        broadcast_weights(model, src=0)  # the one NCCL collective of the run
-    model.packed(device)
-    return model
+    if name == "attn_micro":
+        return microbench.attention_inputs(cfg, count, start)
+    return microbench.conv19_inputs(cfg, count, start)
+
+
+def bench_config(name: str, cfg: dict, world: int) -> dict:
+    """The `config` object of the JSON line; the same for both arms."""
+
+    base = {"global_batch": cfg["batch"], "parallelism": f"position-sharded x{world}",
+            "l2": "flushed (256 MB write) between timed steps"}
+    n = disk_cells(cfg["disk"])
+    if name in FORWARD_CONFIGS:
+        return {"workload": f"{name}-size ShrimpNet.forward_policy_value", **base,
+                "channels": cfg["channels"], "heads": cfg["attention_heads"], "trunk_layout": cfg["trunk_layout"],
+                "cells": n, "seq_len": n + 8, "weights": "NCCL-broadcast once", "cuda_graph": True}
+    if name == "attn_micro":
+        return {"workload": "biased-attention microbench (sb_offset_attention)", **base, "tokens": n,
+                "heads": cfg["heads"], "head_dim": cfg["head_dim"],
+                "table_rows": disk_cells(cfg["table_radius"]), "dtype_io": "bf16"}
+    return {"workload": "19-tap ray conv microbench (sb_raytap_conv)", **base, "cells": n,
+            "channels": cfg["channels"], "taps": 19, "dtype_io": "bf16"}
+
+
+def data_note(name: str, cfg: dict) -> str:
+    if name in FORWARD_CONFIGS:
+        return (f"synthetic: seeded uniform-random legal play on the radius-{cfg['disk']} disk, "
+                f"0-{cfg['plies']} plies, random-init weights (seed {cfg['seed']})")
+    return f"synthetic: seeded N(0,1) activations and seeded tables/weights (seed {cfg['seed']})"
+
+
+# ---- CPU reference (both arms) --------------------------------------------------
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def time_reference_cpu(name: str, cfg: dict, steps: int, warmup: int) -> dict:
+    """The oracle port of the reference path (fp32 torch on every host thread
+    this process may use) on a fixed sample of the workload: `warmup` untimed
+    calls, then `steps` timed calls. One function for the reference arm and for
+    the native line's cpu_baseline, so both report the same measurement."""
+
+    from oracle import forward as oracle
+
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    sample = min(cfg["cpu_sample"], cfg["batch"])
+    if name in FORWARD_CONFIGS:
+        from hexo_bot_b200.model import ShrimpNet
+
+        kw = {k: cfg[k] for k in ("channels", "attention_heads", "trunk_layout")}
+        torch.manual_seed(cfg["seed"])
+        sd = ShrimpNet(**kw).state_dict()
+        batch = make_batch(cfg, sample, 0)
+        a = (batch["feats"], batch["nbr"], batch["mask"], batch["coords"])
+        call = lambda: oracle.forward_policy_value(sd, *a, heads=kw["attention_heads"], layout=kw["trunk_layout"])
+        what = f"{sample} positions per call, oracle forward_policy_value (fp32 torch CPU)"
+    elif name == "attn_micro":
+        m = micro_inputs(name, cfg, sample, 0)
+        q, k, v = (m[x].float() for x in ("q", "k", "v"))
+        call = lambda: oracle.offset_bias_attention(q, k, v, m["table"], m["offset_map"], cfg["heads"]).bfloat16()
+        what = f"{sample} positions per call, oracle offset_bias_attention (fp32 torch CPU, bf16 out)"
+    else:
+        m = micro_inputs(name, cfg, sample, 0)
+        x = m["x"].float()
+        call = lambda: oracle.raytap_conv(x, m["nbr"], m["weight"].float(), m["bias"]).bfloat16()
+        what = f"{sample} positions per call, oracle raytap_conv (fp32 torch CPU, bf16 out)"
+    with torch.no_grad():
+        for _ in range(max(warmup, 1)):
+            call()
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            call()
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    return {"value": sample * steps / total, "sample": sample, "threads": threads, "ms_per_call": total / steps * 1e3,
+            "median_ms": statistics.median(times) * 1e3, "what": what}
+
+
+def reference_line(args, name: str, cfg: dict, r: dict) -> dict:
+    value = round(r["value"], 2)
+    return {
+        "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms_per_call"], 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": data_note(name, cfg), "config": bench_config(name, cfg, args.gpus),
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "positions/s", "cores": r["threads"], "kind": "port",
+                         "sample": f"{r['what']}; {r['threads']} threads; median call {r['median_ms']:.1f} ms"},
+        "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def run_reference(args, name: str, cfg: dict):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    r = time_reference_cpu(name, cfg, args.steps, args.warmup)
+    print(json.dumps(reference_line(args, name, cfg, r)), flush=True)
+
+
+def cpu_baseline(name: str, steps: int = 10, warmup: int = 3) -> dict | None:
+    """The reference arm's measurement, run as a fresh child process (no CUDA
+    context, no distributed environment) so it sees the host exactly as the
+    `--impl reference` run does."""
+
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT",
+                        "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID")}
+    env["CUDA_VISIBLE_DEVICES"] = ""
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--config", name, "--steps", str(steps),
+           "--warmup", str(warmup)]
+    proc = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT, timeout=900)
+    lines = [l for l in proc.stdout.splitlines() if l.startswith("{")]
+    if proc.returncode != 0 or not lines:
+        return {"value": None, "error": proc.stderr[-400:]}
+    d = json.loads(lines[-1])
+    cb = dict(d["cpu_baseline"])
+    cb["sample"] += f"; {steps} timed calls after {warmup} warm-up (bench.py --impl reference, child process)"
+    return cb
+
+
+# ---- GPU timing -------------------------------------------------------------------
 
 
 def flush_l2(buf: torch.Tensor):
@@ -155,186 +294,39 @@ def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor) -> list[float]:
     return out
 
 
-def cpu_baseline(cfg: dict, budget_s: float = 12.0) -> dict:
-    """The CPU restatement of the reference forward (fp32, all host threads) on
-    a bounded sample of the workload."""
-
-    from oracle import forward as oracle
-    from hexo_bot_b200.model import ShrimpNet
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    kw = {k: cfg[k] for k in ("channels", "attention_heads", "trunk_layout")}
-    torch.manual_seed(cfg["seed"])
-    sd = ShrimpNet(**kw).state_dict()
-    sample = 256 if cfg["batch"] >= 256 else cfg["batch"]
-    batch = make_batch(cfg, sample, 0)
-    args = (batch["feats"], batch["nbr"], batch["mask"], batch["coords"])
-    oracle.forward_policy_value(sd, *args, heads=kw["attention_heads"], layout=kw["trunk_layout"])
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or len(times) < 3:
-        t0 = time.perf_counter()
-        oracle.forward_policy_value(sd, *args, heads=kw["attention_heads"], layout=kw["trunk_layout"])
-        times.append(time.perf_counter() - t0)
-        if len(times) >= 50:
-            break
-    med = statistics.median(times)
-    return {
-        "value": round(sample / med, 2),
-        "unit": "positions/s",
-        "cores": threads,
-        "kind": "port",
-        "sample": f"{sample} positions of the same workload per call, median of {len(times)} calls "
-                  f"({med * 1e3:.0f} ms each), fp32 torch CPU",
-    }
-
-
-def run_reference(args, cfg):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    from oracle import forward as oracle
-    from hexo_bot_b200.model import ShrimpNet
-
-    kw = {k: cfg[k] for k in ("channels", "attention_heads", "trunk_layout")}
-    torch.manual_seed(cfg["seed"])
-    sd = ShrimpNet(**kw).state_dict()
-    sample = 128 if cfg["batch"] >= 128 else cfg["batch"]
-    batch = make_batch(cfg, sample, 0)
-    a = (batch["feats"], batch["nbr"], batch["mask"], batch["coords"])
-    call = lambda: oracle.forward_policy_value(sd, *a, heads=kw["attention_heads"], layout=kw["trunk_layout"])
-    for _ in range(args.warmup):
-        call()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        call()
-        times.append(time.perf_counter() - t0)
-    total = sum(times)
-    value = sample * args.steps / total
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "positions/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": f"synthetic: seeded uniform-random legal play on the radius-{cfg['disk']} disk, "
-                f"0-{cfg['plies']} plies, random-init weights (seed {cfg['seed']})",
-        "config": {"workload": f"{args.config} forward_policy_value (CPU reference restatement)",
-                   "global_batch": cfg["batch"], "sample_per_step": sample},
-        "impl": "reference",
-        "cpu_baseline": {"value": round(value, 2), "unit": "positions/s", "cores": threads, "kind": "port",
-                         "sample": f"{sample} positions per step, fp32 torch CPU, {threads} threads"},
-        "e2e": {"value": round(value, 2), "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-
-
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["native", "reference"], default="native")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="main")
-    ap.add_argument("--batch", type=int, default=None, help="override the global batch")
-    ap.add_argument("--no-latency", action="store_true")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["conv"], default=None,
-                    help="time only the dominant kernel at the bench shape (for profiling)")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
-    cfg = dict(CONFIGS[args.config])
-    if args.batch:
-        cfg["batch"] = args.batch
-
-    if args.impl == "reference":
-        run_reference(args, cfg)
-        return
-
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-
-    from hexo_bot_b200 import _lib
-    from hexo_bot_b200.model import ShrimpNet
-
-    total = cfg["batch"]
-    from hexo_bot_b200.sharding import shard_range
-
-    lo, hi = shard_range(total, rank, world)
-    shard = hi - lo
-    host = make_batch(cfg, shard, lo)
-    model = build_model(cfg, device, rank, world)
-    npad = host["feats"].shape[1]
-    dev_in = [host[k].to(device) for k in ("feats", "nbr", "mask", "coords")]
-    if args.kernel == "conv":
-        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-        r = conv_roofline(model, dev_in, cfg, shard, npad, device, flush, steps=args.steps, warmup=args.warmup)
-        if rank == 0:
-            print(json.dumps({"kernel_only": r}), flush=True)
-        return
-    out = {
-        "policy": torch.empty(shard, npad, dtype=torch.float32, device=device),
-        "value": torch.empty(shard, 65, dtype=torch.float32, device=device),
-    }
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-
-    def fwd():
-        model.forward_policy_value(*dev_in, out=out)
-
-    # capture the whole forward once as a CUDA graph (serve mode)
-    fwd()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        fwd()
-    step = graph.replay
-
-    sampler = ClockSampler(local) if rank == 0 else None
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    if sampler:
-        sampler.start()
-    times = time_steps(step, args.steps, args.warmup, flush)
-    clocks = sampler.stop() if sampler else None
-    torch.cuda.synchronize()
-    ms = statistics.mean(times)
+def max_over_ranks(ms: float, device, world: int) -> float:
     t = torch.tensor([ms], device=device, dtype=torch.float64)
     if world > 1:
-        dist.barrier()
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = total / (ms_max / 1e3)
+    return float(t.item())
 
-    # ---- end to end: pinned host inputs -> H2D -> forward -> D2H, every step ----
-    # A serving loop: the copies of step s+1's inputs and of step s's outputs
-    # run on a copy stream while the forward of step s runs (two device input
-    # and output sets). Every step's H2D and D2H is inside the timed region,
-    # which spans all K steps (one event pair around the loop, no L2 flush:
-    # each step's inputs arrive from the host and the forward's working set,
-    # ~1.3 GB at B=4096, is larger than L2).
-    feats_h = host["feats"].half().pin_memory()
-    nbr_h = torch.where(host["nbr"] >= npad, torch.full_like(host["nbr"], 0xFFFF), host["nbr"]).to(
-        torch.int32).to(torch.uint16).pin_memory()
-    mask_h = host["mask"].pin_memory()
-    coords_h = host["coords"].to(torch.int16).pin_memory()
-    host_in = (feats_h, nbr_h, mask_h, coords_h)
-    e2e_in = [[torch.empty_like(x, device=device) for x in host_in] for _ in range(2)]
-    e2e_out = [{"policy": torch.empty(shard, npad, dtype=torch.float32, device=device),
-                "value": torch.empty(shard, 65, dtype=torch.float32, device=device)} for _ in range(2)]
-    pol_h = [torch.empty(shard, npad, dtype=torch.float32).pin_memory() for _ in range(2)]
-    val_h = [torch.empty(shard, 65, dtype=torch.float32).pin_memory() for _ in range(2)]
+
+def build_model(cfg: dict, device, world: int):
+    from hexo_bot_b200.model import ShrimpNet
+    from hexo_bot_b200.sharding import broadcast_weights
+
+    kw = {k: cfg[k] for k in ("channels", "attention_heads", "trunk_layout")}
+    torch.manual_seed(cfg["seed"])
+    model = ShrimpNet(**kw).to(device)
+    if world > 1:
+        broadcast_weights(model, src=0)  # the one NCCL collective of the run
+    model.packed(device)
+    return model
+
+
+def e2e_serving_loop(call, host_in: list, host_out: list, make_dev_out, device, steps: int, warmup: int) -> float:
+    """ms per step of a serving loop through the public call with HOST buffers:
+    the H2D of step s+1's inputs and the D2H of step s's outputs run on a copy
+    stream while step s computes (two device input / output sets). Every step's
+    copies are inside the timed region, one event pair around all steps."""
+
+    dev_in = [[torch.empty_like(x, device=device) for x in host_in] for _ in range(2)]
+    dev_out = [make_dev_out() for _ in range(2)]
+    host_o = [[torch.empty_like(x).pin_memory() for x in host_out] for _ in range(2)]
     main_st = torch.cuda.current_stream()
     copy_st = torch.cuda.Stream()
 
-    def e2e_run(k: int) -> float:
+    def run(k: int) -> float:
         h2d_ev = [torch.cuda.Event() for _ in range(2)]
         fwd_ev = [torch.cuda.Event() for _ in range(2)]
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -345,8 +337,8 @@ def main():
             b = step % 2
             with torch.cuda.stream(copy_st):
                 if step >= 2:
-                    copy_st.wait_event(fwd_ev[b])  # the forward that last read buffer b
-                for d, h in zip(e2e_in[b], host_in):
+                    copy_st.wait_event(fwd_ev[b])  # the step that last read buffer b
+                for d, h in zip(dev_in[b], host_in):
                     d.copy_(h, non_blocking=True)
                 h2d_ev[b].record(copy_st)
 
@@ -356,83 +348,121 @@ def main():
             if step + 1 < k:
                 h2d(step + 1)
             main_st.wait_event(h2d_ev[b])
-            model.forward_policy_value(*e2e_in[b], out=e2e_out[b])
+            call(dev_in[b], dev_out[b])
             fwd_ev[b].record(main_st)
             with torch.cuda.stream(copy_st):
                 copy_st.wait_event(fwd_ev[b])
-                pol_h[b].copy_(e2e_out[b]["policy"], non_blocking=True)
-                val_h[b].copy_(e2e_out[b]["value"], non_blocking=True)
+                for h, d in zip(host_o[b], dev_out[b]):
+                    h.copy_(d, non_blocking=True)
         main_st.wait_stream(copy_st)
         end.record(main_st)
         end.synchronize()
         return start.elapsed_time(end) / k
 
-    e2e_run(args.warmup)
+    run(warmup)
     torch.cuda.synchronize()
-    t2 = torch.tensor([e2e_run(args.steps)], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
-    e2e_value = total / (float(t2.item()) / 1e3)
-    h2d = sum(x.numel() * x.element_size() for x in host_in)
-    d2h = pol_h[0].numel() * 4 + val_h[0].numel() * 4
+    return run(steps)
 
-    # ---- dominant kernel: the ConvBlock gather-GEMM at the bench shape ----
+
+# ---- forward bench ----------------------------------------------------------------
+
+
+def run_forward(args, name, cfg, rank, world, local, device):
+    from hexo_bot_b200.model import ShrimpNet
+    from hexo_bot_b200.sharding import shard_range
+
+    total = cfg["batch"]
+    lo, hi = shard_range(total, rank, world)
+    shard = hi - lo
+    host = make_batch(cfg, shard, lo)
+    model = build_model(cfg, device, world)
+    npad = host["feats"].shape[1]
+    dev_in = [host[k].to(device) for k in ("feats", "nbr", "mask", "coords")]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    if args.kernel == "conv":
+        r = conv_roofline(model, dev_in, name, cfg, shard, npad, device, flush, steps=args.steps, warmup=args.warmup)
+        if rank == 0:
+            print(json.dumps({"kernel_only": r}), flush=True)
+        return
+    out = {
+        "policy": torch.empty(shard, npad, dtype=torch.float32, device=device),
+        "value": torch.empty(shard, 65, dtype=torch.float32, device=device),
+    }
+
+    def fwd():
+        model.forward_policy_value(*dev_in, out=out)
+
+    # capture the whole forward once as a CUDA graph (serve mode)
+    fwd()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fwd()
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    times = time_steps(graph.replay, args.steps, args.warmup, flush)
+    clocks = sampler.stop() if sampler else None
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_max = max_over_ranks(statistics.mean(times), device, world)
+    value = total / (ms_max / 1e3)
+
+    # ---- end to end: pinned host inputs -> H2D -> forward -> D2H, every step ----
+    feats_h = host["feats"].half().pin_memory()
+    nbr_h = torch.where(host["nbr"] >= npad, torch.full_like(host["nbr"], 0xFFFF), host["nbr"]).to(
+        torch.int32).to(torch.uint16).pin_memory()
+    mask_h = host["mask"].pin_memory()
+    coords_h = host["coords"].to(torch.int16).pin_memory()
+    host_in = [feats_h, nbr_h, mask_h, coords_h]
+    host_out = [torch.empty(shard, npad, dtype=torch.float32), torch.empty(shard, 65, dtype=torch.float32)]
+
+    def e2e_call(d_in, d_out):
+        model.forward_policy_value(*d_in, out={"policy": d_out[0], "value": d_out[1]})
+
+    def e2e_out():
+        return [torch.empty(shard, npad, dtype=torch.float32, device=device),
+                torch.empty(shard, 65, dtype=torch.float32, device=device)]
+
+    e2e_ms = max_over_ranks(e2e_serving_loop(e2e_call, host_in, host_out, e2e_out, device, args.steps, args.warmup),
+                            device, world)
+    e2e_value = total / (e2e_ms / 1e3)
+    h2d = sum(x.numel() * x.element_size() for x in host_in)
+    d2h = sum(x.numel() * x.element_size() for x in host_out)
+
     roofline = None
     if rank == 0:
-        roofline = conv_roofline(model, dev_in, cfg, shard, npad, device, flush)
-
+        roofline = conv_roofline(model, dev_in, name, cfg, shard, npad, device, flush)
     extra = {}
-    if rank == 0 and world == 1 and not args.no_latency and args.config == "main":
+    if rank == 0 and world == 1 and not args.no_latency and name == "main":
         extra["latency_p50_ms"] = latency_sweep(model, cfg, device)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(cfg)
+    cpu = cpu_baseline(name) if rank == 0 and world == 1 and not args.no_cpu_baseline else None
 
     if rank == 0:
-        launches = ShrimpNet.kernel_launches(cfg["trunk_layout"]) * args.steps
+        peaks = load_peaks()
+        tflops = cfg["mflop"] * 1e6 * total / (ms_max / 1e3) / 1e12 / world
         line = {
-            "metric": METRIC,
-            "value": round(value, 1),
-            "unit": "positions/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(ms_max, 4),
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "f16",
-            "data": f"synthetic: seeded uniform-random legal play on the radius-{cfg['disk']} disk, "
-                    f"0-{cfg['plies']} plies, random-init weights (seed {cfg['seed']})",
-            "config": {
-                "workload": f"{args.config}-size ShrimpNet.forward_policy_value",
-                "global_batch": total,
-                "channels": cfg["channels"],
-                "heads": cfg["attention_heads"],
-                "trunk_layout": cfg["trunk_layout"],
-                "cells": npad,
-                "seq_len": npad + 8,
-                "parallelism": f"position-sharded x{world}, weights NCCL-broadcast once",
-                "l2": "flushed (256 MB write) between timed steps",
-                "cuda_graph": True,
-            },
+            "metric": METRIC, "value": round(value, 1), "unit": "positions/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": data_note(name, cfg), "config": bench_config(name, cfg, world),
             "roofline": roofline,
             "model_roofline": {
-                "bound": "tensor",
-                "achieved": round(cfg["mflop"] * 1e6 * total / (ms_max / 1e3) / 1e12 / world, 2),
-                "peak": load_peaks()["tflops_sustained"],
-                "unit": "TFLOP/s per GPU",
-                "frac": round(cfg["mflop"] * 1e6 * total / (ms_max / 1e3) / 1e12 / world
-                              / load_peaks()["tflops_sustained"], 4),
-                "note": f"{cfg['mflop']} MFLOP/position algorithmic, vs sustained bf16 peak "
-                        f"({load_peaks()['source']})",
+                "bound": "tensor", "achieved": round(tflops, 2), "peak": peaks["tflops_sustained"],
+                "unit": "TFLOP/s per GPU", "frac": round(tflops / peaks["tflops_sustained"], 4),
+                "note": f"{cfg['mflop']} MFLOP/position algorithmic, vs sustained bf16 peak ({peaks['source']})",
             },
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "positions/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h),
                     "note": "public module call per step; H2D of the next step and D2H of this step on a "
                             "copy stream overlapping the forward; timed over all steps"},
-            "gpu_launches": launches,
+            "gpu_launches": ShrimpNet.kernel_launches(cfg["trunk_layout"]) * args.steps,
             "clocks": clocks,
         }
         line.update(extra)
@@ -440,12 +470,11 @@ def main():
     if world > 1:
         del graph
         dist.barrier()
-        dist.destroy_process_group()
 
 
-def conv_roofline(model, dev_in, cfg, shard, npad, device, flush, steps=20, warmup=3) -> dict:
-    """Time the trunk's gather-GEMM conv (conv + LN + ReLU epilogue, the kernel
-    that carries ~70 % of the FLOPs) alone at the bench shape via the C ABI."""
+def conv_roofline(model, dev_in, name, cfg, shard, npad, device, flush, steps=20, warmup=3) -> dict:
+    """Time the trunk's 7-tap conv (conv + LN + ReLU epilogue, the kernel that
+    carries ~70 % of the FLOPs) alone at the bench shape via the C ABI."""
 
     import ctypes as C
 
@@ -471,12 +500,16 @@ def conv_roofline(model, dev_in, cfg, shard, npad, device, flush, steps=20, warm
     bias = blk.conv1.bias.detach().float().contiguous()
     lw = blk.ln1.weight.detach().float().contiguous()
     lb = blk.ln1.bias.detach().float().contiguous()
+    kernel_stream = torch.cuda.current_stream()
 
     def call():
         _lib.check(lib.sb_hex_conv_ln(x.data_ptr(), gidx.data_ptr(), mask.data_ptr(), wp.data_ptr(), bias.data_ptr(),
                                       lw.data_ptr(), lb.data_ptr(), 1e-5, 1, shard, npad, c, c, out.data_ptr(),
-                                      ws.data_ptr(), nb.value, torch.cuda.current_stream().cuda_stream), "conv")
+                                      ws.data_ptr(), nb.value, kernel_stream.cuda_stream), "conv")
 
+    # The call also runs two small table kernels (absolute gather rows, row
+    # mask: a few microseconds); they stay inside the timed region, so the
+    # conv's own rate is slightly above the reported one.
     times = time_steps(call, steps, warmup, flush)
     ms = statistics.mean(times)
     flops = 2.0 * shard * npad * 7 * c * c
@@ -489,7 +522,7 @@ def conv_roofline(model, dev_in, cfg, shard, npad, device, flush, steps=20, warm
         "peak": peaks["tflops"],
         "unit": "TFLOP/s",
         "frac": round(achieved / peaks["tflops"], 4),
-        "traffic": DOMINANT_TRAFFIC_BYTES,
+        "traffic": DOMINANT_TRAFFIC_BYTES.get((name, shard)),
         "algorithmic_flop_per_launch": flops,
         "ms_per_launch": round(ms, 4),
         "peak_source": f"bf16_tflops burst, {peaks['source']} (f16 runs at the same tensor rate)",
@@ -524,6 +557,141 @@ def latency_sweep(model, cfg, device) -> dict:
         res[str(b)] = round(statistics.median(ts), 4)
         del g
     return res
+
+
+# ---- microbench lines -------------------------------------------------------------
+
+
+def run_micro(args, name, cfg, rank, world, local, device):
+    """One kernel call per step through the C ABI at the microbench shape."""
+
+    from hexo_bot_b200 import _lib
+    from hexo_bot_b200.sharding import shard_range
+
+    lib = _lib.lib()
+    total = cfg["batch"]
+    lo, hi = shard_range(total, rank, world)
+    shard = hi - lo
+    m = micro_inputs(name, cfg, shard, lo)
+    n = disk_cells(cfg["disk"])
+    st = torch.cuda.current_stream()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    peaks = load_peaks()
+    if name == "attn_micro":
+        h, d = cfg["heads"], cfg["head_dim"]
+        table = m["table"].to(device)
+        om = m["offset_map"].to(device)
+        rows = table.shape[0]
+        host_in = [m["q"].pin_memory(), m["k"].pin_memory(), m["v"].pin_memory()]
+        dev = [x.to(device) for x in host_in]
+        out = torch.empty_like(dev[0])
+
+        def call(d_in, d_out):
+            _lib.check(lib.sb_offset_attention(d_in[0].data_ptr(), d_in[1].data_ptr(), d_in[2].data_ptr(),
+                                               table.data_ptr(), rows, om.data_ptr(), shard, n, h, d,
+                                               d_out[0].data_ptr(), st.cuda_stream), "sb_offset_attention")
+
+        launches = 1
+        algo = 4 * shard * n * h * d * 2 + table.numel() * 4 + om.numel() * 4  # q, k, v read + out write
+        bound, unit, peak = "hbm", "GB/s", peaks["hbm_gbs"]
+        kname = "attn_kernel (OFFSET bias mode)"
+    else:
+        c = cfg["channels"]
+        taps = m["nbr"].shape[1]
+        nbr = m["nbr"].to(device)
+        wp = m["weight"].t().contiguous().to(device)  # [Cout][taps*Cin], K-major
+        bias = m["bias"].to(device)
+        ws = torch.empty(shard * n * taps * 4 + 64, dtype=torch.uint8, device=device)
+        host_in = [m["x"].pin_memory()]
+        dev = [host_in[0].to(device)]
+        out = torch.empty_like(dev[0])
+
+        def call(d_in, d_out):
+            _lib.check(lib.sb_raytap_conv(d_in[0].data_ptr(), nbr.data_ptr(), taps, wp.data_ptr(), bias.data_ptr(),
+                                          shard, n, c, d_out[0].data_ptr(), ws.data_ptr(), ws.numel(),
+                                          st.cuda_stream), "sb_raytap_conv")
+
+        launches = 2
+        algo = 2.0 * shard * n * taps * c * c
+        bound, unit, peak = "tensor", "TFLOP/s", peaks["tflops"]
+        kname = "gemm_ws_kernel (19-tap gather-GEMM, bias + residual + ReLU epilogue)"
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    times = time_steps(lambda: call(dev, [out]), args.steps, args.warmup, flush)
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        dist.barrier()
+    ms_max = max_over_ranks(statistics.mean(times), device, world)
+    value = total / (ms_max / 1e3)
+    achieved = algo / (statistics.mean(times) / 1e3) / (1e9 if bound == "hbm" else 1e12)
+    host_out = [torch.empty_like(host_in[0])]
+    e2e_ms = max_over_ranks(
+        e2e_serving_loop(call, host_in, host_out, lambda: [torch.empty_like(dev[0])], device, args.steps,
+                         args.warmup), device, world)
+    cpu = cpu_baseline(name) if rank == 0 and world == 1 and not args.no_cpu_baseline else None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "positions/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": data_note(name, cfg), "config": bench_config(name, cfg, world),
+            "roofline": {"kernel": kname, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "algorithmic_per_launch": algo, "ms_per_launch": round(statistics.mean(times), 4),
+                         "peak_source": peaks["source"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(total / (e2e_ms / 1e3), 1), "unit": "positions/s",
+                    "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in host_in)),
+                    "d2h_bytes_per_step": int(host_out[0].numel() * host_out[0].element_size())},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="main")
+    ap.add_argument("--batch", type=int, default=None, help="override the global batch")
+    ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["conv"], default=None,
+                    help="time only the dominant kernel at the bench shape (for profiling)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    name = args.config
+    cfg = dict(CONFIGS[name])
+    if args.batch:
+        cfg["batch"] = args.batch
+
+    if args.impl == "reference":
+        run_reference(args, name, cfg)
+        return
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    try:
+        if name in FORWARD_CONFIGS:
+            run_forward(args, name, cfg, rank, world, local, device)
+        else:
+            run_micro(args, name, cfg, rank, world, local, device)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":

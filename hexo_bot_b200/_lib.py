@@ -67,7 +67,7 @@ class Net(C.Structure):
         ("tokens", _P), ("tokens_ln16", _P),
         ("ln_final_w", _P), ("ln_final_b", _P),
         ("policy_conv_w", _P), ("policy_conv_b", _P),
-        ("policy_head_w", _P), ("policy_head_b", C.c_float),
+        ("policy_head_w", _P), ("policy_head_b", _P),
         ("value_red_wT", _P), ("value_red_b", _P), ("value_head_wT", _P), ("value_head_b", _P),
         ("ml_red_wT", _P), ("ml_red_b", _P), ("ml_head_wT", _P), ("ml_head_b", _P),
         ("lut", _P),

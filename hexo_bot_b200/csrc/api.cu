@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -188,41 +189,6 @@ int make_tmap_3d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int es
   return SB_OK;
 }
 
-// Operand producer of the tensor-core GEMM: 0 = TMA (gather4 rows + 2D weight
-// tiles) whenever the shapes allow it, 1 = cp.async everywhere. Read once from
-// SHRIMP_B200_GEMM_PRODUCER ("tma" | "cpasync").
-int producer_mode() {
-  static int mode = -1;
-  if (mode < 0) {
-    const char* e = getenv("SHRIMP_B200_GEMM_PRODUCER");
-    mode = (e && strcmp(e, "cpasync") == 0) ? 1 : 0;
-  }
-  return mode;
-}
-
-// Epilogue of identity-row GEMMs: 0 = TMA-staged stores (default), 1 = per-row
-// stores (SHRIMP_B200_EPILOGUE=lsu, for comparison runs).
-int epilogue_mode() {
-  static int mode = -1;
-  if (mode < 0) {
-    const char* e = getenv("SHRIMP_B200_EPILOGUE");
-    mode = (e && strcmp(e, "lsu") == 0) ? 1 : 0;
-  }
-  return mode;
-}
-
-// Attention core for short sequences of head_dim 16: 0 = the geometry-cached
-// kernel (default), 1 = the general position-resident kernel
-// (SHRIMP_B200_ATTN=resident, for comparison runs).
-int attn_mode() {
-  static int mode = -1;
-  if (mode < 0) {
-    const char* e = getenv("SHRIMP_B200_ATTN");
-    mode = (e && strcmp(e, "resident") == 0) ? 1 : 0;
-  }
-  return mode;
-}
-
 int num_sms() {
   static int cache[64] = {0};
   int dev = 0;
@@ -257,7 +223,7 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
   memset(&ma, 0, sizeof(ma));
   memset(&mb, 0, sizeof(mb));
   a.use_tma = (a.cin % kChunkK == 0) && (a.lda % 8 == 0) && ((uintptr_t)a.A % 16 == 0) &&
-              ((uintptr_t)a.Bw % 16 == 0) && a.a_rows < (1LL << 31) - 1 && producer_mode() != 1;
+              ((uintptr_t)a.Bw % 16 == 0) && a.a_rows < (1LL << 31) - 1;
   if (a.use_tma) {
     if (int s = make_tmap(&ma, a.A, bf16, a.lda, a.a_rows, a.lda, a.gidx ? 1 : kBlockM)) return s;
     if (int s = make_tmap(&mb, a.Bw, bf16, a.kpad, a.n_total, a.kpad, a.bn)) return s;
@@ -270,7 +236,7 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
   memset(&m32b, 0, sizeof(m32b));
   a.tma_epi = a.use_tma && !a.gidx && (a.bn / 2) % 32 == 0 && !(a.flags & (EPI_HEAD | EPI_RES16)) &&
               ((uintptr_t)a.out16 % 16 == 0) && ((uintptr_t)a.out32 % 16 == 0) && ((uintptr_t)a.out32b % 16 == 0) &&
-              (a.ld16 * 2) % 16 == 0 && (a.ld32 * 4) % 16 == 0 && (a.ld32b * 4) % 16 == 0 && epilogue_mode() == 0;
+              (a.ld16 * 2) % 16 == 0 && (a.ld32 * 4) % 16 == 0 && (a.ld32b * 4) % 16 == 0;
   if (a.tma_epi) {
     const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     if (a.flags & EPI_OUT16)
@@ -322,7 +288,7 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
   if (a.taps != 7 || !a.gidx || (a.cin != C && !narrow) || C % 64 || 2 * C + 64 > 512 || cells <= 0 ||
       cells > kBlockM || xrows < cells)
     return 1;
-  if (a.lda != a.cin || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16 || producer_mode() == 1) return 1;
+  if (a.lda != a.cin || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16) return 1;
   // positions per tile: 4, 2 or 1 (each position owns 128 / ppt TMEM lanes)
   int ppt = 4;
   while (ppt > 1 && (cells > kBlockM / ppt || ppt * xrows > 256)) ppt >>= 1;
@@ -404,7 +370,7 @@ int launch_attention(AttnArgs a, cudaStream_t st) {
   const int dp = round_up(a.D, 16);
   // Geometry-cached kernel: head_dim 16, whole 64-column boxes of heads,
   // q | k | v as the column blocks of one row-major buffer.
-  if (attn_mode() == 0 && a.mode == BIAS_COORDS && a.D == kGeoD && a.H % 4 == 0 && a.S > a.ntok &&
+  if (a.mode == BIAS_COORDS && a.D == kGeoD && a.H % 4 == 0 && a.S > a.ntok &&
       a.S <= kGeoMaxS && 2 * (a.S - a.ntok) + a.S <= kGeoThreads && a.table_rows <= 255 && a.coords && a.lut) {
     const long long C = (long long)a.H * a.D;
     const T* q = reinterpret_cast<const T*>(a.q);
@@ -499,6 +465,13 @@ int launch_attention(AttnArgs a, cudaStream_t st) {
 // Readable bytes kept after every gather table (the GEMM prefetches it in
 // whole 16-byte pieces).
 constexpr size_t kGidxSlack = 64;
+
+// Workspace of the hex_conv entry points for `rows` = batch * npad cells: the
+// absolute gather table (7 int32 per row, plus the prefetch slack, rounded to
+// 256 bytes) followed by the fp32 row mask.
+constexpr size_t hex_conv_workspace_for(size_t rows) {
+  return ((rows * 7 * 4 + kGidxSlack + 255) & ~size_t(255)) + rows * 4;
+}
 
 struct FwdLayout {
   size_t seq32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, total;
@@ -779,8 +752,7 @@ int sb_build_pair_u8(const void* coords, int coords_dtype, const void* mask, int
 
 int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes) {
   if (!bytes || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "hex_conv workspace: bad args");
-  const size_t rows = (size_t)batch * npad;
-  *bytes = ((rows * 7 * 4 + kGidxSlack + 255) & ~size_t(255)) + rows * 4;
+  *bytes = hex_conv_workspace_for((size_t)batch * npad);
   return SB_OK;
 }
 
@@ -824,6 +796,10 @@ int sb_hex_conv(const void* x, const int32_t* gather_idx, const uint8_t* mask, c
 // library still allocates nothing at run time.
 constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB: up to 262,141 rows (batch * npad)
 constexpr long long kNoAllocMaxRows = 262141;       // largest batch * npad whose workspace fits
+static_assert(hex_conv_workspace_for(kNoAllocMaxRows) <= kNoAllocScratchBytes,
+              "the documented row limit must fit the fixed scratch");
+static_assert(hex_conv_workspace_for(kNoAllocMaxRows + 1) > kNoAllocScratchBytes,
+              "the documented row limit must be the largest that fits");
 static __device__ __align__(256) uint8_t g_hex_conv_scratch[kNoAllocScratchBytes];
 
 int sb_hex_conv_noalloc(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w,
@@ -837,20 +813,23 @@ int sb_hex_conv_noalloc(const void* x, const int32_t* gather_idx, const uint8_t*
                 "(at most %lld rows)",
                 (long long)batch * npad, need, kNoAllocScratchBytes, kNoAllocMaxRows);
   // Per-device symbol address, resolved on the first call on each device
-  // (that call does the set-up; later calls only read the cache).
-  static void* scratch[64] = {nullptr};
+  // (that call does the set-up; later calls only read the cache). Threads
+  // racing on a first call all store the same address; the entries are
+  // atomic so that race is benign. The cache is not refreshed after
+  // cudaDeviceReset.
+  static std::atomic<void*> scratch[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(SB_ERR_CUDA, "hex_conv_noalloc: no current device");
-  if (!scratch[dev]) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_hex_conv_scratch);
-    if (e != cudaSuccess || !ptr)
+  void* base = scratch[dev].load(std::memory_order_relaxed);
+  if (!base) {
+    const cudaError_t e = cudaGetSymbolAddress(&base, g_hex_conv_scratch);
+    if (e != cudaSuccess || !base)
       return fail(SB_ERR_CUDA, "hex_conv_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    scratch[dev] = ptr;
+    scratch[dev].store(base, std::memory_order_relaxed);
   }
   return hex_conv_common(x, gather_idx, mask, w, bias, nullptr, nullptr, 0.f, 0, batch, npad, cin, cout, out,
-                         scratch[dev], kNoAllocScratchBytes, stream);
+                         base, kNoAllocScratchBytes, stream);
 }
 
 int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w, const float* bias,

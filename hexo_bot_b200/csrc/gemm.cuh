@@ -93,7 +93,7 @@ struct GemmArgs {
   const void* res16;       // 16-bit residual rows (microbench)
   long long ldr16;
   const float* head_w;
-  float head_b;
+  const float* head_b;     // [1] (EPI_HEAD)
   float* head_out;
   int seq_len;             // rows per position in the seq layout (for EPI_LNB_TOKENS)
   int ntok;
@@ -184,7 +184,7 @@ __device__ __forceinline__ void stats_merge(float& cnt, float& mean, float& m2, 
 
 // Exact (erf) GELU, x * Phi(x), without erff: Phi(x) = 1 - h (x >= 0) or h
 // (x < 0) with h = 0.5 * exp(-z^2) * R(z), z = min(|x| / sqrt(2), 4), and R a
-// degree-11 polynomial fit of exp(z^2) * erfc(z) on [0, 4] (csrc/fit_gelu.py
+// degree-11 polynomial fit of exp(z^2) * erfc(z) on [0, 4] (tests/fit_gelu.py
 // produces the coefficients and checks the error: at most ~8e-7 absolute
 // against 0.5 * x * (1 + erf(x / sqrt(2))) over all float32 x). Straight-line
 // code: 11 FMAs of Horner, one exp2 on the special-function unit, no branch.
@@ -539,7 +539,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const EpiVecs& 
     asm volatile("bar.sync %0, 64;\n" ::"r"(bar_id) : "memory");
     head = half ? xot->x + head : head + xot->x;
     asm volatile("bar.sync %0, 64;\n" ::"r"(bar_id) : "memory");
-    if (a.head_out) st_global_f32_if(a.head_out + r.mc, r.mk * (head + a.head_b), r.valid && half == 0);
+    if (a.head_out) st_global_f32_if(a.head_out + r.mc, r.mk * (head + __ldg(a.head_b)), r.valid && half == 0);
   }
 
   if (HEAVY && (fl & EPI_LN_B)) {

@@ -75,6 +75,46 @@ def cell_bias_lut() -> np.ndarray:
     return lut
 
 
+# --- microbench tables (BASELINE configs 2 and 3; no reference kernel) -----------
+
+# Win axes in the order [Q, R, QR] (hexfield_eq features.py:79 AXIS_DELTAS).
+RAY_AXES = ((1, 0), (0, 1), (1, -1))
+RAY_STEPS = 3
+RAY_TAPS = 1 + len(RAY_AXES) * 2 * RAY_STEPS  # 19
+
+
+def raytap_neighbors(disk_radius: int) -> np.ndarray:
+    """(N, 19) int32 over the radius-`disk_radius` disk in `disk_offsets` order:
+    tap 0 is the cell itself; tap 1 + axis*6 + dir*3 + (k-1) is the cell at
+    offset (+k or -k for dir 0 / 1) x axis, -1 when that cell is off the disk
+    (the ray packing of hexfield_eq _raytap.py:84-96 with three steps)."""
+
+    cells = disk_offsets(disk_radius)
+    index = {c: i for i, c in enumerate(cells)}
+    out = np.full((len(cells), RAY_TAPS), -1, dtype=np.int32)
+    for i, (q, r) in enumerate(cells):
+        out[i, 0] = i
+        for a, (aq, ar) in enumerate(RAY_AXES):
+            for d, sgn in enumerate((1, -1)):
+                for k in range(1, RAY_STEPS + 1):
+                    out[i, 1 + a * 6 + d * 3 + (k - 1)] = index.get((q + sgn * k * aq, r + sgn * k * ar), -1)
+    return out
+
+
+def offset_id_map(disk_radius: int, table_radius: int) -> np.ndarray:
+    """(N, N) int32 offset-id map over the radius-`disk_radius` disk: entry
+    (query, key) is the index of the exact offset key - query in
+    `disk_offsets(table_radius)` (217 ids at radius 8, 817 at radius 16)."""
+
+    cells = disk_offsets(disk_radius)
+    ids = {off: i for i, off in enumerate(disk_offsets(table_radius))}
+    out = np.empty((len(cells), len(cells)), dtype=np.int32)
+    for i, (qq, qr) in enumerate(cells):
+        for j, (kq, kr) in enumerate(cells):
+            out[i, j] = ids[(kq - qq, kr - qr)]
+    return out
+
+
 # --- D6 about the origin (geometry.py:52-82) -------------------------------------
 
 

@@ -144,43 +144,81 @@ def _round_up(x: int, m: int) -> int:
 
 class PackedWeights:
     """Device-resident kernel-layout copy of a ShrimpNet's serve weights plus the
-    C `sb_net` descriptor pointing into it."""
+    C `sb_net` descriptor pointing into it.
+
+    Construction allocates every buffer once; `refresh()` re-packs the current
+    parameter values into those same buffers with device work only (no host
+    copy, no synchronisation), so it may run inside CUDA-graph capture and a
+    graph captured earlier keeps valid pointers. fp32 vectors that already
+    live on the device as contiguous fp32 tensors are used in place."""
 
     def __init__(self, model: "ShrimpNet", device: torch.device) -> None:
         self.device = device
         self.keep: list[torch.Tensor] = []
-        lib = _lib.lib()
+        self._ops: list = []  # refresh steps, in order
+        self.packed_in_capture = False
         c, h = model.channels, model.heads
-        stream = torch.cuda.current_stream(device).cuda_stream
         net = _lib.Net()
         net.channels = c
         net.heads = h
         net.num_blocks = len(model._trunk_layout)
         net.layout = model._trunk_layout.encode()
 
+        def live(t: torch.Tensor) -> bool:
+            return t.device == device and t.dtype == torch.float32 and t.is_contiguous()
+
         def f32(t: torch.Tensor) -> int:
-            x = t.detach().to(device=device, dtype=torch.float32).contiguous()
-            self.keep.append(x)
-            return x.data_ptr()
+            """fp32 copy (or the tensor itself when it already is one) of a
+            parameter or of a view of one (e.g. a transpose)."""
+            if live(t):
+                self.keep.append(t)
+                return t.data_ptr()
+            buf = torch.empty(t.shape, dtype=torch.float32, device=device)
+            self.keep.append(buf)
+            self._ops.append(lambda t=t, buf=buf: buf.copy_(t.detach()))
+            return buf.data_ptr()
+
+        def stage(*parts: torch.Tensor) -> torch.Tensor:
+            """fp32 device source of a pack kernel: the parameter itself, or a
+            buffer refreshed from the (concatenated) parameters."""
+            if len(parts) == 1 and live(parts[0]):
+                return parts[0]
+            n = sum(int(x.shape[0]) for x in parts)
+            buf = torch.empty((n,) + tuple(parts[0].shape[1:]), dtype=torch.float32, device=device)
+            self.keep.append(buf)
+
+            def op(parts=parts, buf=buf):
+                off = 0
+                for x in parts:
+                    buf[off:off + x.shape[0]].copy_(x.detach())
+                    off += x.shape[0]
+            self._ops.append(op)
+            return buf
 
         def conv_w(mod: HexNodeConv, cin_pad: int) -> int:
-            w = mod.weight.detach().to(device=device, dtype=torch.float32).contiguous()
+            src = stage(mod.weight)
             kpad = _round_up(7 * cin_pad, 64)
             out = torch.empty(mod.out_channels, kpad, dtype=torch.float16, device=device)
-            _lib.check(
-                lib.sb_pack_hex_conv_weight(w.data_ptr(), 7, mod.in_channels, cin_pad, mod.out_channels,
-                                            out.data_ptr(), stream),
-                "sb_pack_hex_conv_weight",
-            )
-            self.keep += [w, out]
+            self.keep.append(out)
+
+            def op(src=src, out=out, mod=mod):
+                _lib.check(_lib.lib().sb_pack_hex_conv_weight(
+                    src.data_ptr(), 7, mod.in_channels, cin_pad, mod.out_channels, out.data_ptr(),
+                    torch.cuda.current_stream(device).cuda_stream), "sb_pack_hex_conv_weight")
+            self._ops.append(op)
             return out.data_ptr()
 
         def lin_w(*weights: torch.Tensor) -> int:
-            w = torch.cat([x.detach() for x in weights], 0).to(device=device, dtype=torch.float32).contiguous()
-            n, k = w.shape
+            src = stage(*weights)
+            n, k = src.shape
             out = torch.empty(n, _round_up(k, 64), dtype=torch.float16, device=device)
-            _lib.check(lib.sb_pack_linear_weight(w.data_ptr(), n, k, out.data_ptr(), stream), "sb_pack_linear_weight")
-            self.keep += [w, out]
+            self.keep.append(out)
+
+            def op(src=src, out=out, n=n, k=k):
+                _lib.check(_lib.lib().sb_pack_linear_weight(src.data_ptr(), n, k, out.data_ptr(),
+                                                            torch.cuda.current_stream(device).cuda_stream),
+                           "sb_pack_linear_weight")
+            self._ops.append(op)
             return out.data_ptr()
 
         net.stem_w = conv_w(model.stem, 16)
@@ -188,18 +226,21 @@ class PackedWeights:
         net.stem_ln_w = f32(model.stem_ln.weight)
         net.stem_ln_b = f32(model.stem_ln.bias)
         net.tokens = f32(model.tokens)
+        # LN1 of the first attention block applied to the learned tokens (the
+        # token rows of that block's input never pass through a conv)
         a0 = model.attn_blocks[0]
-        tok_ln = F.layer_norm(model.tokens.detach().float().cpu(), (c,), a0.ln1.weight.detach().float().cpu(),
-                              a0.ln1.bias.detach().float().cpu(), a0.ln1.eps)
-        tl16 = tok_ln.to(torch.float16).to(device).contiguous()
+        tl16 = torch.empty(K.NUM_TOKENS, c, dtype=torch.float16, device=device)
         self.keep.append(tl16)
+        self._ops.append(lambda: tl16.copy_(F.layer_norm(
+            model.tokens.detach().to(device, torch.float32), (c,), a0.ln1.weight.detach().to(device, torch.float32),
+            a0.ln1.bias.detach().to(device, torch.float32), a0.ln1.eps)))
         net.tokens_ln16 = tl16.data_ptr()
         net.ln_final_w = f32(model.ln_final.weight)
         net.ln_final_b = f32(model.ln_final.bias)
         net.policy_conv_w = conv_w(model.policy_conv, c)
         net.policy_conv_b = f32(model.policy_conv.bias)
         net.policy_head_w = f32(model.policy_head.weight.reshape(-1))
-        net.policy_head_b = float(model.policy_head.bias.detach().float().cpu()[0])
+        net.policy_head_b = f32(model.policy_head.bias)
         net.value_red_wT = f32(model.value_reduction.weight.t())
         net.value_red_b = f32(model.value_reduction.bias)
         net.value_head_wT = f32(model.value_head.weight.t())
@@ -208,7 +249,9 @@ class PackedWeights:
         net.ml_red_b = f32(model.ml_reduction.bias)
         net.ml_head_wT = f32(model.moves_left_head.weight.t())
         net.ml_head_b = f32(model.moves_left_head.bias)
-        lut = torch.from_numpy(cell_bias_lut().copy()).to(device)
+        lut = model._cell_bias_lut_u8
+        if lut.device != device:
+            lut = lut.to(device)
         self.keep.append(lut)
         net.lut = lut.data_ptr()
         for i, blk in enumerate(model.conv_blocks):
@@ -228,7 +271,9 @@ class PackedWeights:
             aw.ln1_w = f32(blk.ln1.weight)
             aw.ln1_b = f32(blk.ln1.bias)
             aw.wqkv = lin_w(at.q_proj.weight, at.k_proj.weight, at.v_proj.weight)
-            aw.bqkv = f32(torch.cat([at.q_proj.bias, at.k_proj.bias, at.v_proj.bias]))
+            qkv_b = stage(at.q_proj.bias, at.k_proj.bias, at.v_proj.bias)
+            self.keep.append(qkv_b)
+            aw.bqkv = qkv_b.data_ptr()
             aw.wo = lin_w(at.out_proj.weight)
             aw.bo = f32(at.out_proj.bias)
             aw.gamma_attn = f32(blk.ls_attn.gamma)
@@ -241,11 +286,25 @@ class PackedWeights:
             aw.gamma_mlp = f32(blk.ls_mlp.gamma)
             # The reference adds the table rounded to fp16 (model.py:741); row
             # BIAS_ROWS is the additive pad-key row.
-            tab = model.bias_tables[i].detach().float().cpu().to(torch.float16).float()
-            pad = torch.full((1, h), K.PAD_KEY_MASK_VALUE)
-            aw.bias_table = f32(torch.cat([tab, pad], 0))
+            tab = torch.empty(K.BIAS_ROWS + 1, h, dtype=torch.float32, device=device)
+            self.keep.append(tab)
+
+            def op(tab=tab, src=model.bias_tables[i]):
+                tab[:K.BIAS_ROWS].copy_(src.detach().to(device).to(torch.float16))
+                tab[K.BIAS_ROWS:].fill_(K.PAD_KEY_MASK_VALUE)
+            self._ops.append(op)
+            aw.bias_table = tab.data_ptr()
         self.net = net
-        torch.cuda.current_stream(device).synchronize()
+        self.refresh()
+
+    def refresh(self) -> None:
+        """Re-pack the current parameter values into this object's buffers on
+        the current stream (device work only)."""
+
+        with torch.no_grad(), torch.autocast(device_type="cuda", enabled=False):
+            for op in self._ops:
+                op()
+        self.packed_in_capture = torch.cuda.is_current_stream_capturing()
 
 
 class ShrimpNet(nn.Module):
@@ -294,9 +353,11 @@ class ShrimpNet(nn.Module):
             "_cell_bias_lut_u8", torch.from_numpy(cell_bias_lut().copy()), persistent=False
         )
         self._init_weights()
-        self._packed: PackedWeights | None = None
-        self._packed_key = None
+        self._packed: dict = {}
+        self._param_list = None
         self._workspace: dict = {}
+        # load_state_dict(assign=True) replaces parameter objects
+        self.register_load_state_dict_post_hook(lambda module, keys: module.invalidate_packed())
 
     def _init_weights(self) -> None:
         """Linear: trunc_normal(0.02) weight, zero bias; LayerNorm: (1, 0);
@@ -323,15 +384,44 @@ class ShrimpNet(nn.Module):
 
     # --- native serve path -------------------------------------------------------
 
-    def _weights_key(self, device: torch.device):
-        return (device, tuple((p.data_ptr(), p._version) for p in self.parameters()))
+    def _apply(self, fn, *args, **kwargs):
+        # .to() / .half() / .cuda() swap parameter storage: build new buffers
+        out = super()._apply(fn, *args, **kwargs)
+        self.invalidate_packed()
+        return out
+
+    def invalidate_packed(self) -> None:
+        """Drop the packed weights; the next forward builds them again. Needed
+        only after replacing parameter objects by hand (assigning a new
+        nn.Parameter): in-place updates, load_state_dict and module
+        conversions are detected on their own."""
+
+        self._packed = {}
+        self._param_list = None
+
+    def _weights_state(self) -> list:
+        if self._param_list is None:
+            self._param_list = list(self.parameters())
+        return [(p.data_ptr(), p._version) for p in self._param_list]
 
     def packed(self, device: torch.device) -> PackedWeights:
-        key = self._weights_key(device)
-        if self._packed is None or self._packed_key != key:
-            self._packed = PackedWeights(self, device)
-            self._packed_key = key
-        return self._packed
+        """The packed weights for `device`, brought up to date: rebuilt when a
+        parameter's storage changed, re-packed in place when only its values
+        changed (in-place update, load_state_dict), and re-packed eagerly once
+        after a pack that was recorded inside a CUDA-graph capture (recorded
+        work runs only when the graph replays)."""
+
+        state = self._weights_state()
+        entry = self._packed.get(device)
+        capturing = torch.cuda.is_current_stream_capturing()
+        if entry is None or [p for p, _ in entry[1]] != [p for p, _ in state]:
+            entry = (PackedWeights(self, device), state)
+            self._packed[device] = entry
+        elif entry[1] != state or (entry[0].packed_in_capture and not capturing):
+            entry[0].refresh()
+            entry = (entry[0], state)
+            self._packed[device] = entry
+        return entry[0]
 
     def _workspace_for(self, device: torch.device, batch: int, npad: int) -> torch.Tensor:
         net = self.packed(device).net
@@ -344,6 +434,7 @@ class ShrimpNet(nn.Module):
             self._workspace[device] = ws
         return ws
 
+    @torch.compiler.disable
     @torch.no_grad()
     def forward_policy_value(
         self,

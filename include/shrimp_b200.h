@@ -98,7 +98,7 @@ typedef struct {
   const void* tokens_ln16;              /* [8][C] f16 = LN1 of the first attention block applied to tokens */
   const float* ln_final_w; const float* ln_final_b;
   const void* policy_conv_w; const float* policy_conv_b;
-  const float* policy_head_w; float policy_head_b;
+  const float* policy_head_w; const float* policy_head_b;  /* [C], [1] */
   const float* value_red_wT; const float* value_red_b;   /* [3C][C], [C] */
   const float* value_head_wT; const float* value_head_b; /* [C][65], [65] */
   const float* ml_red_wT; const float* ml_red_b;
@@ -165,11 +165,12 @@ int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask
  * 8 MiB device array inside the library: batch * npad must be <= 262,141
  * rows, larger calls fail with SB_ERR_UNSUPPORTED. The library allocates
  * nothing (no cudaMalloc / cudaFree). The first call on each device resolves
- * the array's address (set-up; make it before any stream capture); nothing in
- * the scratch needs to start at zero (each call writes what it reads). Calls
- * share the one array per device, so calls that overlap in time on the same
- * device (different streams or threads) race: serialise them. Same results
- * as sb_hex_conv. */
+ * the array's address (set-up; make it before any stream capture) and keeps
+ * it for the life of the process (it is not refreshed after cudaDeviceReset);
+ * nothing in the scratch needs to start at zero (each call writes what it
+ * reads). Calls share the one array per device, so calls that overlap in time
+ * on the same device (different streams or threads) race: serialise them.
+ * Same results as sb_hex_conv. */
 int sb_hex_conv_noalloc(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w_packed,
                         const float* bias, int batch, int npad, int cin, int cout, void* out, void* stream);
 /* Workspace for sb_hex_conv / sb_hex_conv_ln. */

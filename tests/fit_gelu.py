@@ -12,7 +12,7 @@ suffers in float32. R is a degree-11 least-squares fit at 6000 Chebyshev nodes
 of [0, 4]; evaluated in float32 (Horner, exp by exp2) the GELU differs from
 0.5 * x * (1 + erf(x / sqrt(2))) by at most ~8e-7 for every float32 x.
 
-    python hexo_bot_b200/csrc/fit_gelu.py     # prints the coefficients and the error
+    python tests/fit_gelu.py     # prints the coefficients and the error
 """
 
 from math import erf, erfc, sqrt

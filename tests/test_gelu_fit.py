@@ -1,5 +1,5 @@
 """The epilogue's erf-GELU polynomial (csrc/gemm.cuh gelu_erf): the committed
-coefficients are the fit that csrc/fit_gelu.py produces, and the float32
+coefficients are the fit that tests/fit_gelu.py produces, and the float32
 evaluation stays within 1e-6 of the exact GELU that the reference's MLP
 applies (F.gelu, packages/shrimp/python/shrimp/model.py:513)."""
 
@@ -13,7 +13,7 @@ CSRC = Path(__file__).resolve().parents[1] / "hexo_bot_b200" / "csrc"
 
 
 def _fit_module():
-    spec = importlib.util.spec_from_file_location("fit_gelu", CSRC / "fit_gelu.py")
+    spec = importlib.util.spec_from_file_location("fit_gelu", Path(__file__).resolve().parent / "fit_gelu.py")
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod

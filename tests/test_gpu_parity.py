@@ -1,7 +1,7 @@
 """Parity of the native CUDA path against the CPU oracle and the reference's
 golden outputs. Every call goes through the C ABI (hexo_bot_b200._lib).
 
-Tolerances (BASELINE north star): policy logits max-abs <= 2e-2 over real
+Tolerances: policy logits max-abs <= 2e-2 over real
 cells, decoded value max-abs <= 1e-2, legal-prefix policy argmax agreement
 >= 99.5 %; index tables bit-exact.
 """
@@ -361,3 +361,42 @@ def test_decode_kernels_match_oracle():
     torch.cuda.synchronize()
     ref = torch.cat(O.legal_prefix_priors(policy.cpu(), legal))
     assert (pri.cpu() - ref).abs().max().item() <= 1e-6
+
+
+_PDL_CHILD = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[2])
+from hexo_bot_b200 import positions as P
+from hexo_bot_b200.model import ShrimpNet
+from oracle import forward as O
+torch.manual_seed(0)
+m = ShrimpNet(channels=128, attention_heads=8, trunk_layout="CCACCACCACCA")
+m.load_state_dict(O.derandomize(m.state_dict()))
+m = m.to("cuda:0")
+b = P.disk_batch(300, 0, 60, 4)
+out = m.forward_policy_value(*[b[k].to("cuda:0") for k in ("feats", "nbr", "mask", "coords")],
+                             request_moves_left=True)
+torch.save({k: v.cpu() for k, v in out.items()}, sys.argv[1])
+"""
+
+
+def test_programmatic_dependent_launch_gives_identical_results(tmp_path):
+    """SHRIMP_B200_PDL=1 (kernels launched with programmatic stream
+    serialization) changes only launch overlap, never results: the forward of
+    a fresh process with it on is bit-identical to one with it off."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = str(Path(__file__).resolve().parents[1])
+    outs = []
+    for flag in ("0", "1"):
+        path = tmp_path / f"pdl{flag}.pt"
+        env = dict(os.environ, SHRIMP_B200_PDL=flag)
+        proc = subprocess.run([sys.executable, "-c", _PDL_CHILD, str(path), root], env=env, capture_output=True,
+                              text=True, timeout=600)
+        assert proc.returncode == 0, proc.stderr[-2000:]
+        outs.append(torch.load(path))
+    for k in outs[0]:
+        assert torch.equal(outs[0][k], outs[1][k]), k
