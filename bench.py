@@ -54,7 +54,13 @@ MICRO_CONFIGS = {
     "attn_micro": dict(**microbench.ATTN_MICRO, cpu_sample=512),
     "conv19_micro": dict(**microbench.CONV19_MICRO, cpu_sample=256),
 }
-CONFIGS = {**FORWARD_CONFIGS, **MICRO_CONFIGS}
+# The serve path on the reference support (variable node counts): wire
+# payloads through ShrimpEvaluator (plan_groups, device unpack, fused reply).
+SERVE_CONFIGS = {
+    "serve": dict(channels=128, attention_heads=8, trunk_layout="CCACCACCACCA", seed=0, radius=4, plies=60,
+                  batch=256, cpu_sample=16),
+}
+CONFIGS = {**FORWARD_CONFIGS, **MICRO_CONFIGS, **SERVE_CONFIGS}
 METRIC = "Shrimp positions/sec at batch 4096 (1/2/4/8 B200); p50 latency at batch 256"
 LATENCY_BATCHES = (1, 16, 64, 256, 1024)
 # DRAM bytes (read + write) of one launch of the dominant kernel, from an ncu
@@ -150,11 +156,46 @@ def micro_inputs(name: str, cfg: dict, count: int, start: int) -> dict:
     return microbench.conv19_inputs(cfg, count, start)
 
 
+def serve_payload(cfg: dict, count: int, start: int, request_moves_left: bool = True):
+    """Wire payload of seeded reference-support positions [start, start+count)."""
+
+    from hexo_bot_b200 import payload as PL
+    from hexo_bot_b200 import positions
+
+    rows = [positions.support_position(cfg["seed"], start + i, cfg["plies"], cfg["radius"])[:2]
+            for i in range(count)]
+    return PL.build_payload(rows, request_moves_left=request_moves_left)[0]
+
+
+def serve_mflop(payload: dict, cfg: dict) -> float:
+    """Algorithmic MFLOP of the payload's forwards over the real nodes only
+    (padding is waste, not work): stem, 2 convs per ConvBlock, the policy conv,
+    and per AttnBlock the q/k/v/out projections, the MLP and the attention core
+    over S = nodes + 8 tokens."""
+
+    import numpy as np
+
+    c = cfg["channels"]
+    lay = cfg["trunk_layout"]
+    off = np.asarray(payload["node_row_offsets"], dtype=np.float64)
+    n = off[1:] - off[:-1]
+    s = n + 8
+    conv = 2 * n * 7 * c * c
+    flops = 2 * n * 7 * 16 * c + (2 * lay.count("C") + 1) * conv
+    flops = flops + lay.count("A") * (2 * s * c * 4 * c + 2 * s * c * 4 * c + 4 * s * s * c)
+    return float(flops.sum()) / 1e6
+
+
 def bench_config(name: str, cfg: dict, world: int) -> dict:
     """The `config` object of the JSON line; the same for both arms."""
 
     base = {"global_batch": cfg["batch"], "parallelism": f"position-sharded x{world}",
             "l2": "flushed (256 MB write) between timed steps"}
+    if name in SERVE_CONFIGS:
+        return {"workload": "ShrimpEvaluator.evaluate_payload on reference supports (wire payload in, reply out)",
+                **base, "channels": cfg["channels"], "heads": cfg["attention_heads"],
+                "trunk_layout": cfg["trunk_layout"], "support_radius": cfg["radius"], "plies": f"0-{cfg['plies']}",
+                "grouping": "plan_groups (quant 64, waste 0.18, pair ceiling 3.8e7)"}
     n = disk_cells(cfg["disk"])
     if name in FORWARD_CONFIGS:
         return {"workload": f"{name}-size ShrimpNet.forward_policy_value", **base,
@@ -169,6 +210,9 @@ def bench_config(name: str, cfg: dict, world: int) -> dict:
 
 
 def data_note(name: str, cfg: dict) -> str:
+    if name in SERVE_CONFIGS:
+        return (f"synthetic: seeded uniform-random legal play, 0-{cfg['plies']} plies, reference support of radius "
+                f"{cfg['radius']} (variable node counts), random-init weights (seed {cfg['seed']})")
     if name in FORWARD_CONFIGS:
         return (f"synthetic: seeded uniform-random legal play on the radius-{cfg['disk']} disk, "
                 f"0-{cfg['plies']} plies, random-init weights (seed {cfg['seed']})")
@@ -206,6 +250,18 @@ def time_reference_cpu(name: str, cfg: dict, steps: int, warmup: int) -> dict:
         a = (batch["feats"], batch["nbr"], batch["mask"], batch["coords"])
         call = lambda: oracle.forward_policy_value(sd, *a, heads=kw["attention_heads"], layout=kw["trunk_layout"])
         what = f"{sample} positions per call, oracle forward_policy_value (fp32 torch CPU)"
+    elif name in SERVE_CONFIGS:
+        from hexo_bot_b200.model import ShrimpNet
+        from oracle import evaluator as oracle_eval
+
+        kw = {k: cfg[k] for k in ("channels", "attention_heads", "trunk_layout")}
+        torch.manual_seed(cfg["seed"])
+        sd = ShrimpNet(**kw).state_dict()
+        payload = serve_payload(cfg, sample, 0)
+        call = lambda: oracle_eval.evaluate_payload(sd, payload, heads=kw["attention_heads"],  # noqa: E731
+                                                    layout=kw["trunk_layout"])
+        what = (f"{sample} positions per call, oracle evaluate_payload (the reference evaluator's CPU path: "
+                f"plan_groups, per-group pack, fp32 torch forward, decode)")
     elif name == "attn_micro":
         m = micro_inputs(name, cfg, sample, 0)
         q, k, v = (m[x].float() for x in ("q", "k", "v"))
@@ -654,6 +710,100 @@ def run_micro(args, name, cfg, rank, world, local, device):
         print(json.dumps(line), flush=True)
 
 
+# ---- serve path -------------------------------------------------------------------
+
+
+def run_serve(args, name, cfg, rank, world, local, device):
+    """value: sb_evaluate_payload over the rank's payload already on the device
+    (captured as one CUDA graph); e2e: ShrimpEvaluator.evaluate_payload with
+    the wire payload in host memory and the reply bytes back, per step."""
+
+    from hexo_bot_b200.evaluator import ShrimpEvaluator
+    from hexo_bot_b200.sharding import shard_range
+
+    total = cfg["batch"]
+    lo, hi = shard_range(total, rank, world)
+    payload = serve_payload(cfg, hi - lo, lo)
+    model = build_model(cfg, device, world)
+    ev = ShrimpEvaluator(model, device)
+    ev.evaluate_payload(payload)  # warm-up: packs weights, sizes the workspace
+    torch.cuda.synchronize()
+
+    # device-resident variant of the same call: stage once, then time the
+    # evaluate launch sequence alone (graph replay)
+    import numpy as np
+
+    req = ev.stage_payload(payload)
+    groups = req["groups"]
+    offsets = np.asarray(payload["node_row_offsets"], dtype=np.int64)
+    b = req["b"]
+
+    def evaluate():
+        ev.launch(req)
+
+    evaluate()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        evaluate()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    times = time_steps(graph.replay, args.steps, args.warmup, flush)
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        dist.barrier()
+    ms_max = max_over_ranks(statistics.mean(times), device, world)
+    value = total / (ms_max / 1e3)
+
+    # end to end through the public call: payload bytes in, reply bytes out
+    for _ in range(args.warmup):
+        ev.evaluate_payload(payload)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start_ev.record()
+    for _ in range(args.steps):
+        ev.evaluate_payload(payload)
+    end_ev.record()
+    end_ev.synchronize()
+    e2e_ms = max_over_ranks(start_ev.elapsed_time(end_ev) / args.steps, device, world)
+    h2d = req["keep"][0].numel()
+    d2h = 4 * (req["n_out"] + 1)
+    cpu = cpu_baseline(name) if rank == 0 and world == 1 and not args.no_cpu_baseline else None
+    if rank == 0:
+        peaks = load_peaks()
+        mflop = serve_mflop(payload, cfg)
+        tflops = mflop * 1e6 / (ms_max / 1e3) / 1e12
+        sizes = offsets[1:] - offsets[:-1]
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "positions/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": data_note(name, cfg), "config": bench_config(name, cfg, world),
+            "roofline": None,
+            "model_roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peaks["tflops_sustained"],
+                               "unit": "TFLOP/s per GPU", "frac": round(tflops / peaks["tflops_sustained"], 4),
+                               "note": f"{mflop / (hi - lo):.0f} MFLOP/position over real nodes (padding excluded)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(total / (e2e_ms / 1e3), 1), "unit": "positions/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h),
+                    "note": "ShrimpEvaluator.evaluate_payload per step: host staging, plan_groups, one H2D, the "
+                            "group forwards, one D2H and the reply bytes"},
+            "gpu_launches": None,
+            "groups": len(groups),
+            "nodes": {"min": int(sizes.min()), "p50": int(np.median(sizes)), "max": int(sizes.max())},
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -687,6 +837,8 @@ def main():
     try:
         if name in FORWARD_CONFIGS:
             run_forward(args, name, cfg, rank, world, local, device)
+        elif name in SERVE_CONFIGS:
+            run_serve(args, name, cfg, rank, world, local, device)
         else:
             run_micro(args, name, cfg, rank, world, local, device)
     finally:

@@ -25,6 +25,9 @@ EXPORTED = (
     "sb_last_error",
     "sb_forward_workspace_bytes",
     "sb_forward_policy_value",
+    "sb_plan_groups",
+    "sb_evaluate_workspace_bytes",
+    "sb_evaluate_payload",
     "sb_build_gather_index",
     "sb_build_pair_u8",
     "sb_hex_conv",
@@ -90,6 +93,22 @@ class Outputs(C.Structure):
     _fields_ = [(n, _P) for n in ("policy", "value_logits", "value", "ml_logits", "moves_left", "status")]
 
 
+class Payload(C.Structure):
+    _fields_ = [
+        ("node_feats", _P), ("feats_dtype", C.c_int),
+        ("node_qr", _P), ("nbr", _P), ("row_offsets", _P), ("legal_counts", _P), ("prior_offsets", _P),
+        ("batch", C.c_int),
+    ]
+
+
+class Reply(C.Structure):
+    _fields_ = [(n, _P) for n in ("values", "priors", "moves_left", "priors_logits", "status")]
+
+
+class Group(C.Structure):
+    _fields_ = [("start", C.c_int), ("end", C.c_int), ("pad_to", C.c_int)]
+
+
 class NativeError(RuntimeError):
     pass
 
@@ -110,6 +129,10 @@ def lib() -> C.CDLL:
         "sb_last_error": ([C.c_char_p, sz], i32),
         "sb_forward_workspace_bytes": ([C.POINTER(Net), i32, i32, C.POINTER(sz)], i32),
         "sb_forward_policy_value": ([C.POINTER(Net), C.POINTER(Inputs), C.POINTER(Outputs), _P, sz, _P], i32),
+        "sb_plan_groups": ([_P, i32, i32, C.c_double, C.c_double, C.POINTER(Group), C.POINTER(i32)], i32),
+        "sb_evaluate_workspace_bytes": ([C.POINTER(Net), C.POINTER(Group), i32, C.POINTER(sz)], i32),
+        "sb_evaluate_payload": ([C.POINTER(Net), C.POINTER(Payload), C.POINTER(Group), i32, C.POINTER(Reply), _P, sz,
+                                 _P], i32),
         "sb_build_gather_index": ([_P, i32, i32, i32, _P, _P, _P], i32),
         "sb_build_pair_u8": ([_P, i32, _P, i32, i32, i32, _P, _P, _P], i32),
         "sb_hex_conv": ([_P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P, sz, _P], i32),

@@ -370,7 +370,7 @@ int launch_attention(AttnArgs a, cudaStream_t st) {
   const int dp = round_up(a.D, 16);
   // Geometry-cached kernel: head_dim 16, whole 64-column boxes of heads,
   // q | k | v as the column blocks of one row-major buffer.
-  if (a.mode == BIAS_COORDS && a.D == kGeoD && a.H % 4 == 0 && a.S > a.ntok &&
+  if (a.mode == BIAS_COORDS && !a.own_geometry && !a.seq_lens && a.D == kGeoD && a.H % 4 == 0 && a.S > a.ntok &&
       a.S <= kGeoMaxS && 2 * (a.S - a.ntok) + a.S <= kGeoThreads && a.table_rows <= 255 && a.coords && a.lut) {
     const long long C = (long long)a.H * a.D;
     const T* q = reinterpret_cast<const T*>(a.q);
@@ -474,10 +474,12 @@ constexpr size_t hex_conv_workspace_for(size_t rows) {
 }
 
 struct FwdLayout {
-  size_t seq32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, total;
+  size_t seq32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, seqlen;
+  size_t pol32, vlog, mllog;  // payload path only: policy and head logits of a group
+  size_t total;
 };
 
-FwdLayout fwd_layout(int C, int B, int npad) {
+FwdLayout fwd_layout(int C, int B, int npad, bool payload) {
   const size_t S = (size_t)npad + kNumTok;
   const size_t R = (size_t)B * S;
   const size_t Mc = (size_t)B * npad;
@@ -498,6 +500,12 @@ FwdLayout fwd_layout(int C, int B, int npad) {
   L.gidx = take(Mc * 7 * 4 + kGidxSlack);
   L.rowmask = take(R * 4);
   L.coords32 = take(Mc * 2 * 4);
+  L.seqlen = take((size_t)B * 4);
+  if (payload) {
+    L.pol32 = take(Mc * 4);
+    L.vlog = take((size_t)B * kBins * 4);
+    L.mllog = take((size_t)B * kBins * 4);
+  }
   L.total = off;
   return L;
 }
@@ -518,41 +526,27 @@ int validate_net(const sb_net* net) {
   return SB_OK;
 }
 
-}  // namespace
-}  // namespace sb
+// Output and input bindings of one forward over B positions of npad cells.
+struct FwdIo {
+  const PrepArgs* dense;      // the module's (B, Npad, ...) tensors, or
+  const PrepCsrArgs* csr;     // rows [row0, row0 + B) of a serve payload
+  float* policy;              // (B, npad) logits
+  float* value_logits;        // (B, 65)
+  float* value;               // (B) decoded, or NULL
+  float* ml_logits;           // (B, 65), or NULL (moves-left not requested)
+  float* ml;                  // (B) decoded, or NULL
+  const int32_t* legal;       // reply priors (payload path): legal-prefix lengths,
+  const int64_t* prior_offs;  //   flat offsets,
+  float* priors;              //   flat priors (NULL: no reply priors),
+  float* priors_logits;       //   flat raw logits or NULL
+  int* err;
+};
 
-using namespace sb;
-
-extern "C" {
-
-int sb_abi_version(void) { return SB_ABI_VERSION; }
-
-int sb_last_error(char* buf, size_t len) {
-  if (!buf || len == 0) return SB_ERR_INVALID_ARG;
-  snprintf(buf, len, "%s", g_last_error.c_str());
-  return SB_OK;
-}
-
-int sb_forward_workspace_bytes(const sb_net* net, int batch, int npad, size_t* bytes) {
-  if (int s = validate_net(net)) return s;
-  if (!bytes || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "workspace query: bad batch/npad");
-  *bytes = fwd_layout(net->channels, batch, npad).total;
-  return SB_OK;
-}
-
-int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* out, void* workspace,
-                            size_t workspace_bytes, void* stream) {
-  if (int s = validate_net(net)) return s;
-  if (!in || !out || !out->policy || !out->value_logits) return fail(SB_ERR_INVALID_ARG, "inputs/outputs missing");
-  const int B = in->batch, npad = in->npad, C = net->channels, H = net->heads;
-  if (B == 0) return SB_OK;
-  if (B < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "batch=%d npad=%d", B, npad);
-  if (!in->feats || !in->nbr || !in->mask || !in->coords) return fail(SB_ERR_INVALID_ARG, "input pointer NULL");
-  const FwdLayout L = fwd_layout(C, B, npad);
-  if (!workspace || workspace_bytes < L.total)
-    return fail(SB_ERR_WORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, L.total);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+// The serve forward (model.py:972-1003) over one workspace: input staging,
+// stem, the trunk layout, policy conv + head, value / moves-left heads.
+int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t* ws, const FwdIo& io,
+                 cudaStream_t st) {
+  const int C = net->channels, H = net->heads;
   float* seq32 = reinterpret_cast<float*>(ws + L.seq32);
   __half* xa16 = reinterpret_cast<__half*>(ws + L.xa16);
   __half* y16 = reinterpret_cast<__half*>(ws + L.y16);
@@ -563,7 +557,8 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
   int32_t* gidx = reinterpret_cast<int32_t*>(ws + L.gidx);
   float* rowmask = reinterpret_cast<float*>(ws + L.rowmask);
   int32_t* coords32 = reinterpret_cast<int32_t*>(ws + L.coords32);
-  int* err = out->status;
+  int32_t* seqlen = reinterpret_cast<int32_t*>(ws + L.seqlen);
+  int* err = io.err;
 
   const int S = npad + kNumTok;
   const long long R = (long long)B * S;
@@ -573,18 +568,22 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
   const float eps = 1e-5f;
 
   {
-    PrepArgs p{};
-    p.feats = in->feats; p.feats_dtype = in->feats_dtype;
-    p.nbr = in->nbr; p.nbr_dtype = in->nbr_dtype;
-    p.mask = in->mask; p.mask_dtype = in->mask_dtype;
-    p.coords = in->coords; p.coords_dtype = in->coords_dtype;
-    p.B = B; p.npad = npad; p.S = S;
-    p.feat16 = feat16; p.gidx = gidx; p.rowmask = rowmask; p.coords32 = coords32; p.err = err;
-    const long long work = Mc > (long long)B * kNumTok ? Mc : (long long)B * kNumTok;
     // the first kernel waits for everything before it in the stream (inputs,
     // weight packing); the ones after it chain programmatically
-    prep_cells_kernel<<<(unsigned)cdiv(work, 256), 256, 0, st>>>(p);
-    if (int s = check_launch("prep_cells_kernel")) return s;
+    const long long work = Mc > (long long)B * kNumTok ? Mc : (long long)B * kNumTok;
+    if (io.csr) {
+      PrepCsrArgs p = *io.csr;
+      p.B = B; p.npad = npad; p.S = S;
+      p.feat16 = feat16; p.gidx = gidx; p.rowmask = rowmask; p.coords32 = coords32; p.seq_lens = seqlen; p.err = err;
+      prep_csr_kernel<<<(unsigned)cdiv(work, 256), 256, 0, st>>>(p);
+      if (int s = check_launch("prep_csr_kernel")) return s;
+    } else {
+      PrepArgs p = *io.dense;
+      p.B = B; p.npad = npad; p.S = S;
+      p.feat16 = feat16; p.gidx = gidx; p.rowmask = rowmask; p.coords32 = coords32; p.err = err;
+      prep_cells_kernel<<<(unsigned)cdiv(work, 256), 256, 0, st>>>(p);
+      if (int s = check_launch("prep_cells_kernel")) return s;
+    }
   }
   PdlScope pdl_scope(true);
   {
@@ -669,6 +668,9 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
       at.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
       at.mode = BIAS_COORDS; at.table = w.bias_table; at.table_rows = SB_BIAS_ROWS + 1;
       at.coords = coords32; at.keymask = rowmask; at.lut = net->lut; at.err = err;
+      // payload groups: live length per position (dead key / query tiles
+      // skipped) and a geometry of its own per position (no shared cache)
+      if (io.csr) { at.seq_lens = seqlen; at.own_geometry = 1; }
       if (int s = launch_attention<__half>(at, st)) return s;
       // out_proj, gamma * mask residual; LN2 for the MLP (model.py:511-512)
       GemmArgs go = linear_args(o16, C, w.wo, C, w.bo);
@@ -699,7 +701,7 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
   // policy: (relu(conv(cells)) . w + b) * mask (model.py:1011-1020)
   {
     GemmArgs g = conv_args(xa16, net->policy_conv_w, net->policy_conv_b);
-    g.flags = EPI_HEAD; g.head_w = net->policy_head_w; g.head_b = net->policy_head_b; g.head_out = out->policy;
+    g.flags = EPI_HEAD; g.head_w = net->policy_head_w; g.head_b = net->policy_head_b; g.head_out = io.policy;
     if (int s = launch_conv<__half>(g, B, npad, S, st)) return s;
   }
   // value (+ moves-left) heads and decode (model.py:984-1003, losses.py:40-61)
@@ -707,10 +709,14 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
     HeadsArgs h{};
     h.lnf16 = xa16; h.rowmask = rowmask; h.B = B; h.S = S; h.C = C;
     h.vr_wT = net->value_red_wT; h.vr_b = net->value_red_b; h.vh_wT = net->value_head_wT; h.vh_b = net->value_head_b;
-    h.value_logits = out->value_logits; h.value = out->value;
-    if (out->ml_logits) {
+    h.value_logits = io.value_logits; h.value = io.value;
+    if (io.ml_logits) {
       h.mr_wT = net->ml_red_wT; h.mr_b = net->ml_red_b; h.mh_wT = net->ml_head_wT; h.mh_b = net->ml_head_b;
-      h.ml_logits = out->ml_logits; h.ml = out->moves_left;
+      h.ml_logits = io.ml_logits; h.ml = io.ml;
+    }
+    if (io.priors) {
+      h.policy = io.policy; h.npad = npad; h.legal = io.legal; h.prior_offs = io.prior_offs;
+      h.priors = io.priors; h.priors_logits = io.priors_logits;
     }
     // positions per CTA: 4, or 8 once four per CTA would take more than
     // two waves (fewer re-reads of the layer-1 weights)
@@ -726,6 +732,150 @@ int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* 
       launch_ex(heads_kernel<8>, grid, kHeadsThreads, smem, st, h);
     if (int s = check_launch("heads_kernel")) return s;
   }
+  return SB_OK;
+}
+
+
+}  // namespace
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" {
+
+int sb_abi_version(void) { return SB_ABI_VERSION; }
+
+int sb_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return SB_ERR_INVALID_ARG;
+  snprintf(buf, len, "%s", g_last_error.c_str());
+  return SB_OK;
+}
+
+int sb_forward_workspace_bytes(const sb_net* net, int batch, int npad, size_t* bytes) {
+  if (int s = validate_net(net)) return s;
+  if (!bytes || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "workspace query: bad batch/npad");
+  *bytes = fwd_layout(net->channels, batch, npad, false).total;
+  return SB_OK;
+}
+
+int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* out, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (int s = validate_net(net)) return s;
+  if (!in || !out || !out->policy || !out->value_logits) return fail(SB_ERR_INVALID_ARG, "inputs/outputs missing");
+  const int B = in->batch, npad = in->npad;
+  if (B == 0) return SB_OK;
+  if (B < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "batch=%d npad=%d", B, npad);
+  if (!in->feats || !in->nbr || !in->mask || !in->coords) return fail(SB_ERR_INVALID_ARG, "input pointer NULL");
+  if ((long long)B * (npad + kNumTok) > (1LL << 31) - 1) return fail(SB_ERR_UNSUPPORTED, "batch too large");
+  const FwdLayout L = fwd_layout(net->channels, B, npad, false);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SB_ERR_WORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, L.total);
+  PrepArgs p{};
+  p.feats = in->feats; p.feats_dtype = in->feats_dtype;
+  p.nbr = in->nbr; p.nbr_dtype = in->nbr_dtype;
+  p.mask = in->mask; p.mask_dtype = in->mask_dtype;
+  p.coords = in->coords; p.coords_dtype = in->coords_dtype;
+  FwdIo io{};
+  io.dense = &p;
+  io.policy = out->policy; io.value_logits = out->value_logits; io.value = out->value;
+  io.ml_logits = out->ml_logits; io.ml = out->ml_logits ? out->moves_left : nullptr;
+  io.err = out->status;
+  return forward_body(net, B, npad, L, reinterpret_cast<uint8_t*>(workspace), io,
+                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ---- serve payload: ShrimpEvaluator.submit_payload / result ------------------
+
+int sb_plan_groups(const int64_t* row_offsets, int batch, int quant, double waste_fraction, double pair_ceiling,
+                   sb_group* groups, int* num_groups) {
+  if (!row_offsets || !groups || !num_groups || batch < 0 || quant <= 0)
+    return fail(SB_ERR_INVALID_ARG, "plan_groups: bad args");
+  int ng = 0, start = 0;
+  while (start < batch) {
+    const long long first = row_offsets[start + 1] - row_offsets[start];
+    const long long pad_to = first <= quant ? quant : (first + quant - 1) / quant * quant;
+    const long long waste = (long long)(waste_fraction * (double)pad_to);  // truncation, as int()
+    const long long floor_size = pad_to - (waste > quant ? waste : quant);
+    const double s2 = (double)(pad_to + kNumTok) * (double)(pad_to + kNumTok);
+    int end = start + 1;
+    while (end < batch) {
+      if ((double)(end - start + 1) * s2 > pair_ceiling) break;
+      if (row_offsets[end + 1] - row_offsets[end] < floor_size) break;
+      ++end;
+    }
+    for (int r = start; r < end; ++r)
+      if (row_offsets[r + 1] - row_offsets[r] > pad_to || row_offsets[r + 1] < row_offsets[r])
+        return fail(SB_ERR_INVALID_ARG,
+                    "plan_groups: row %d has %lld nodes > the group's %lld; rows must come sorted by node count, "
+                    "largest first (the payload order)", r, (long long)(row_offsets[r + 1] - row_offsets[r]), pad_to);
+    if (pad_to > (1 << 20)) return fail(SB_ERR_UNSUPPORTED, "plan_groups: row of %lld nodes", first);
+    groups[ng].start = start;
+    groups[ng].end = end;
+    groups[ng].pad_to = (int)pad_to;
+    ++ng;
+    start = end;
+  }
+  *num_groups = ng;
+  return SB_OK;
+}
+
+int sb_evaluate_workspace_bytes(const sb_net* net, const sb_group* groups, int num_groups, size_t* bytes) {
+  if (int s = validate_net(net)) return s;
+  if (!bytes || num_groups < 0 || (num_groups > 0 && !groups)) return fail(SB_ERR_INVALID_ARG, "evaluate workspace");
+  size_t need = 0;
+  for (int i = 0; i < num_groups; ++i) {
+    const int g = groups[i].end - groups[i].start;
+    if (g <= 0 || groups[i].pad_to <= 0) return fail(SB_ERR_INVALID_ARG, "evaluate workspace: group %d", i);
+    const size_t t = fwd_layout(net->channels, g, groups[i].pad_to, true).total;
+    need = t > need ? t : need;
+  }
+  *bytes = need;
+  return SB_OK;
+}
+
+int sb_evaluate_payload(const sb_net* net, const sb_payload* payload, const sb_group* groups, int num_groups,
+                        sb_reply* reply, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int s = validate_net(net)) return s;
+  if (!payload || !reply || num_groups < 0 || (num_groups > 0 && !groups))
+    return fail(SB_ERR_INVALID_ARG, "evaluate: payload/reply/groups missing");
+  if (payload->batch == 0) return SB_OK;
+  if (!payload->node_feats || !payload->node_qr || !payload->nbr || !payload->row_offsets ||
+      !payload->legal_counts || !payload->prior_offsets || !reply->values || !reply->priors)
+    return fail(SB_ERR_INVALID_ARG, "evaluate: NULL payload or reply pointer");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  int covered = 0;
+  for (int i = 0; i < num_groups; ++i) {
+    const sb_group& gr = groups[i];
+    const int g = gr.end - gr.start;
+    if (gr.start != covered || g <= 0 || gr.end > payload->batch || gr.pad_to <= 0)
+      return fail(SB_ERR_INVALID_ARG, "evaluate: groups must tile rows 0..%d in order (group %d)", payload->batch, i);
+    covered = gr.end;
+    if ((long long)g * (gr.pad_to + kNumTok) > (1LL << 31) - 1) return fail(SB_ERR_UNSUPPORTED, "group too large");
+    const FwdLayout L = fwd_layout(net->channels, g, gr.pad_to, true);
+    if (!workspace || workspace_bytes < L.total)
+      return fail(SB_ERR_WORKSPACE, "evaluate: workspace %zu < required %zu bytes", workspace_bytes, L.total);
+    PrepCsrArgs p{};
+    p.feats = payload->node_feats; p.feats_dtype = payload->feats_dtype;
+    p.qr = payload->node_qr; p.nbr = payload->nbr; p.offsets = payload->row_offsets; p.row0 = gr.start;
+    FwdIo io{};
+    io.csr = &p;
+    io.policy = reinterpret_cast<float*>(ws + L.pol32);
+    io.value_logits = reinterpret_cast<float*>(ws + L.vlog);
+    io.value = reply->values + gr.start;
+    if (reply->moves_left) {
+      io.ml_logits = reinterpret_cast<float*>(ws + L.mllog);
+      io.ml = reply->moves_left + gr.start;
+    }
+    io.legal = payload->legal_counts + gr.start;
+    io.prior_offs = payload->prior_offsets + gr.start;
+    io.priors = reply->priors;
+    io.priors_logits = reply->priors_logits;
+    io.err = reply->status;
+    if (int s = forward_body(net, g, gr.pad_to, L, ws, io, st)) return s;
+  }
+  if (covered != payload->batch) return fail(SB_ERR_INVALID_ARG, "evaluate: groups cover %d of %d rows", covered,
+                                             payload->batch);
   return SB_OK;
 }
 

@@ -52,9 +52,11 @@ struct AttnArgs {
   const float* keymask;   // BIAS_COORDS: [B][S] (1 = live key); nullptr = all live
   const uint8_t* lut;     // BIAS_COORDS: [35*35]
   const uint8_t* pair;    // BIAS_PAIR: [B][S][S]
-  const int32_t* seq_lens;  // BIAS_PAIR: [B] live sequence length (keys and queries beyond it
-                            // are padding: skipped / written as zeros); nullptr = S
+  const int32_t* seq_lens;  // [B] live sequence length, or nullptr = S: keys beyond it are
+                            // skipped and query rows beyond it are written as zeros (PAIR:
+                            // the reference op's seq_lens; COORDS: rows [live cells | pad])
   const int32_t* offset_map;  // BIAS_OFFSET: [S][S]
+  int own_geometry;           // BIAS_COORDS: positions do not share one cell set (no geometry cache)
   int group;              // heads staged per pass (set by the host)
   int* err;               // device status word (SB_DEV_ERR_* bits), or nullptr
 };
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
     const T* Vb = reinterpret_cast<const T*>(a.v) + (long long)b * a.pos_stride;
     T* Ob = reinterpret_cast<T*>(a.out) + (long long)b * a.out_pos_stride;
     int n_keys = S;
-    if (a.mode == BIAS_PAIR && a.seq_lens) n_keys = max(0, min(S, __ldg(a.seq_lens + b)));
+    if (a.seq_lens) n_keys = max(0, min(S, __ldg(a.seq_lens + b)));
 
     // stage Q, K, V of heads [h0, h0 + gh) (zero rows >= S, zero columns >= D)
     auto stage = [&](int h0, int gh) {
@@ -281,7 +283,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
           for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
         float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 
-        for (int k0 = 0; k0 < n_keys; k0 += KB) {
+        // query tiles wholly past the live length do no work (written as zeros)
+        const int key_end = qt * 16 < n_keys ? n_keys : 0;
+        for (int k0 = 0; k0 < key_end; k0 += KB) {
           float s[NT][4];
           float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
@@ -436,7 +440,16 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
   const T* Q = reinterpret_cast<const T*>(a.q) + hoff;
   const T* Kg = reinterpret_cast<const T*>(a.k) + hoff;
   const T* Vg = reinterpret_cast<const T*>(a.v) + hoff;
-  const int n_live = (a.mode == BIAS_PAIR && a.seq_lens) ? max(0, min(S, __ldg(a.seq_lens + b))) : S;
+  const int n_live = a.seq_lens ? max(0, min(S, __ldg(a.seq_lens + b))) : S;
+  // a query block wholly past the live length: zeros, no key pass
+  if (qblk * kStreamBlockQ >= n_live) {
+    T* Ob = reinterpret_cast<T*>(a.out) + (long long)b * a.out_pos_stride + (long long)h * a.out_head_stride;
+    for (int i = tid; i < kStreamBlockQ * D; i += kStreamThreads) {
+      const int row = qblk * kStreamBlockQ + i / D;
+      if (row < S) reinterpret_cast<uint16_t*>(Ob)[(long long)row * a.out_row_stride + i % D] = 0;  // +0.0
+    }
+    return;
+  }
   float* table_s = reinterpret_cast<float*>(smem + SM::kOffTable);
   uint8_t* lut_s = smem + SM::kOffLut;
 
@@ -480,7 +493,7 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
     for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 
-  const int nkb = (S + kStreamBlockK - 1) / kStreamBlockK;
+  const int nkb = (n_live + kStreamBlockK - 1) / kStreamBlockK;  // key blocks past the live length: skipped
   const int pieces = DP / 8;  // 16-byte pieces per row (padded)
   auto load_block = [&](int kb, int buf) {
     const uint32_t sK = smem_u32(smem + SM::kOffK + buf * SM::kTileBytes);
@@ -500,7 +513,7 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
       float live = key < n_live ? 1.f : 0.f;
       int2 c = make_int2(0, 0);
       if (key < S && key >= a.ntok) {
-        if (a.keymask) live = __ldg(a.keymask + (long long)b * S + key);
+        if (a.keymask && key < n_live) live = __ldg(a.keymask + (long long)b * S + key);
         if (a.mode == BIAS_COORDS) {
           const int32_t* cp = a.coords + ((long long)b * (S - a.ntok) + (key - a.ntok)) * 2;
           c = make_int2(__ldg(cp), __ldg(cp + 1));

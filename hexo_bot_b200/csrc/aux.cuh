@@ -58,6 +58,24 @@ struct PrepArgs {
   int* err;
 };
 
+// Inputs of one group of rows of the serve payload (the evaluator's wire ABI,
+// shrimp-rs payload.rs:108-158): CSR over support nodes, rows [row0, row0 + B)
+// padded to npad cells each.
+struct PrepCsrArgs {
+  const void* feats; int feats_dtype;  // (total_nodes, 15)
+  const int16_t* qr;                   // (total_nodes, 2) hex coordinates
+  const uint16_t* nbr;                 // (total_nodes, 6) row-local neighbours, 0xFFFF = missing
+  const int64_t* offsets;              // (rows + 1) first node of each payload row
+  int row0;
+  int B, npad, S;
+  __half* feat16;
+  int32_t* gidx;
+  float* rowmask;
+  int32_t* coords32;
+  int32_t* seq_lens;  // (B) 8 tokens + the row's node count: rows past it are padding
+  int* err;
+};
+
 // One thread per cell: stage features (f16, padded to 16 channels), the
 // absolute-row gather table (tap 0 = self, taps 1..6 = DIRECTIONS neighbours;
 // reference trunk gather_idx, model.py:860-863), the row mask and int32 coords.
@@ -94,6 +112,59 @@ __global__ void prep_cells_kernel(const PrepArgs a) {
     a.coords32[2 * i + 1] = (int32_t)load_index(a.coords, a.coords_dtype, 2 * i + 1);
   }
   // token rows of the row mask
+  if (i < (long long)a.B * kNumTok) {
+    const long long b = i / kNumTok, t = i - b * kNumTok;
+    a.rowmask[b * a.S + t] = 1.f;
+  }
+}
+
+// prep_cells_kernel for one group of payload rows: node n of row b is cell n
+// of position b (the support order [legal | stones | halo] is kept), cells past
+// the row's node count are padding (zero features, no neighbours, mask 0,
+// coordinates 0: the reference evaluator's per-group pack, inference.py:865-897).
+__global__ void prep_csr_kernel(const PrepCsrArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long ncell = (long long)a.B * a.npad;
+  if (i < ncell) {
+    const int b = (int)(i / a.npad);
+    const int n = (int)(i - (long long)b * a.npad);
+    const long long o0 = __ldg(a.offsets + a.row0 + b);
+    const long long size = __ldg(a.offsets + a.row0 + b + 1) - o0;
+    const long long row = (long long)b * a.S + kNumTok + n;
+    const bool real = n < size;
+    const long long node = o0 + n;
+    __align__(16) __half f[kFeatPad];
+#pragma unroll
+    for (int c = 0; c < kNumFeat; ++c)
+      f[c] = __float2half_rn(real ? load_float(a.feats, a.feats_dtype, node * kNumFeat + c) : 0.f);
+    f[kNumFeat] = __float2half_rn(0.f);
+    uint4* dst = reinterpret_cast<uint4*>(a.feat16 + row * kFeatPad);
+    dst[0] = reinterpret_cast<const uint4*>(f)[0];
+    dst[1] = reinterpret_cast<const uint4*>(f)[1];
+    int32_t* g = a.gidx + i * 7;
+    g[0] = (int32_t)row;
+    for (int k = 0; k < 6; ++k) {
+      int32_t out = -1;
+      if (real) {
+        const int v = __ldg(a.nbr + node * 6 + k);
+        if (v < size && v < a.npad) {
+          out = (int32_t)((long long)b * a.S + kNumTok + v);
+        } else if (v != 0xFFFF && a.err) {
+          atomicOr(a.err, 2);
+        }
+      }
+      g[1 + k] = out;
+    }
+    a.rowmask[row] = real ? 1.f : 0.f;
+    a.coords32[2 * i] = real ? (int32_t)__ldg(a.qr + 2 * node) : 0;
+    a.coords32[2 * i + 1] = real ? (int32_t)__ldg(a.qr + 2 * node + 1) : 0;
+    if (n == 0) {
+      if (size > a.npad && a.err) atomicOr(a.err, 4);
+      a.seq_lens[b] = kNumTok + (int)min(size, (long long)a.npad);
+    }
+  }
   if (i < (long long)a.B * kNumTok) {
     const long long b = i / kNumTok, t = i - b * kNumTok;
     a.rowmask[b * a.S + t] = 1.f;
@@ -204,6 +275,14 @@ struct HeadsArgs {
   float* value_logits; float* value;
   const float* mr_wT; const float* mr_b; const float* mh_wT; const float* mh_b;
   float* ml_logits; float* ml;
+  // serve reply (optional): legal-prefix softmax of each position's policy
+  // logits written flat at prior_offs[b] (inference.py:998-1042)
+  const float* policy;        // (B, npad) logits
+  int npad;
+  const int32_t* legal;       // (B) legal-prefix lengths
+  const int64_t* prior_offs;  // (B) flat offsets
+  float* priors;              // flat priors, or NULL (no reply)
+  float* priors_logits;       // flat raw logits at the same offsets, or NULL
 };
 
 constexpr int kHeadsThreads = 256;
@@ -431,6 +510,31 @@ __device__ void heads_pass(const HeadsArgs& a, int pass, float* sm, int b0, int 
   __syncthreads();  // shared buffers are reused by the next pass
 }
 
+// One warp per position: softmax over the first legal[b] policy logits,
+// written flat (with the raw logits when asked) at prior_offs[b].
+__device__ void heads_priors(const HeadsArgs& a, int b0, int npos) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int p = warp; p < npos; p += kHeadsThreads / 32) {
+    const int b = b0 + p;
+    const int L = min(__ldg(a.legal + b), a.npad);
+    const float* row = a.policy + (long long)b * a.npad;
+    float mx = -INFINITY;
+    for (int i = lane; i < L; i += 32) mx = fmaxf(mx, row[i]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float se = 0.f;
+    for (int i = lane; i < L; i += 32) se += expf(row[i] - mx);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+    const long long off = __ldg(a.prior_offs + b);
+    for (int i = lane; i < L; i += 32) {
+      const float x = row[i];
+      a.priors[off + i] = expf(x - mx) / se;
+      if (a.priors_logits) a.priors_logits[off + i] = x;
+    }
+  }
+}
+
 template <int P>
 __global__ void __launch_bounds__(kHeadsThreads) heads_kernel(const HeadsArgs a) {
   extern __shared__ __align__(16) float hsm[];
@@ -439,6 +543,7 @@ __global__ void __launch_bounds__(kHeadsThreads) heads_kernel(const HeadsArgs a)
   const int npos = min(P, a.B - b0);
   heads_pass<P>(a, 0, hsm, b0, npos);
   if (a.ml_logits) heads_pass<P>(a, 1, hsm, b0, npos);
+  if (a.priors) heads_priors(a, b0, npos);  // policy logits come from an earlier kernel (after pdl_wait)
 }
 
 __global__ void decode_binned_kernel(const float* logits, int B, float scale, float offset, float* out) {

@@ -356,8 +356,11 @@ class ShrimpNet(nn.Module):
         self._packed: dict = {}
         self._param_list = None
         self._workspace: dict = {}
-        # load_state_dict(assign=True) replaces parameter objects
-        self.register_load_state_dict_post_hook(lambda module, keys: module.invalidate_packed())
+        self._retired_workspaces: list = []
+        # load_state_dict(assign=True) replaces parameter objects: re-read the
+        # parameter list (an in-place load keeps the packed buffers, which are
+        # re-packed in place, so graphs captured before it stay valid)
+        self.register_load_state_dict_post_hook(lambda module, keys: setattr(module, "_param_list", None))
 
     def _init_weights(self) -> None:
         """Linear: trunc_normal(0.02) weight, zero bias; LayerNorm: (1, 0);
@@ -394,7 +397,9 @@ class ShrimpNet(nn.Module):
         """Drop the packed weights; the next forward builds them again. Needed
         only after replacing parameter objects by hand (assigning a new
         nn.Parameter): in-place updates, load_state_dict and module
-        conversions are detected on their own."""
+        conversions are detected on their own. Like a module conversion
+        (.to / .half), this frees buffers that CUDA graphs captured before it
+        point to: capture those graphs again."""
 
         self._packed = {}
         self._param_list = None
@@ -430,7 +435,13 @@ class ShrimpNet(nn.Module):
                    "sb_forward_workspace_bytes")
         ws = self._workspace.get(device)
         if ws is None or ws.numel() < nbytes.value:
-            ws = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=device)
+            # A CUDA graph captured with the old workspace keeps its address, so
+            # the old one stays allocated (retired); growing by at least 1.5x
+            # bounds the retired bytes by twice the final size.
+            if ws is not None:
+                self._retired_workspaces.append(ws)
+            size = max(nbytes.value, 1 if ws is None else int(ws.numel() * 1.5))
+            ws = torch.empty(size, dtype=torch.uint8, device=device)
             self._workspace[device] = ws
         return ws
 

@@ -65,6 +65,7 @@ typedef enum {
 /* Status-word bits written by kernels (caller-provided int32 on the device). */
 #define SB_DEV_ERR_TIMEOUT 1    /* a bounded mbarrier wait gave up */
 #define SB_DEV_ERR_NBR_RANGE 2  /* a neighbour index was > Npad (treated as missing) */
+#define SB_DEV_ERR_ROW_SIZE 4   /* a payload row has more nodes than its group's pad_to (truncated) */
 
 /* ---- weights ----------------------------------------------------------------
  * Device pointers into caller-owned packed weights. "hw" = f16 [N][Kpad]
@@ -136,6 +137,49 @@ int sb_last_error(char* buf, size_t len);
 int sb_forward_workspace_bytes(const sb_net* net, int batch, int npad, size_t* bytes);
 int sb_forward_policy_value(const sb_net* net, const sb_inputs* in, sb_outputs* out, void* workspace,
                             size_t workspace_bytes, void* stream);
+
+/* ---- serve payload: ShrimpEvaluator.submit_payload + result ---------------
+ * (inference.py:509-604, 807-863, 865-1042; wire ABI shrimp-rs payload.rs:108-158)
+ * The evaluator's request, already on the device: rows are positions, sorted
+ * by node count (largest first), their support nodes concatenated (CSR). */
+typedef struct {
+  const void* node_feats; int feats_dtype;  /* (total_nodes, 15) f16 on the wire (f32 / bf16 accepted) */
+  const int16_t* node_qr;                   /* (total_nodes, 2) hex coordinates (q, r) */
+  const uint16_t* nbr;                      /* (total_nodes, 6) row-local neighbour index, 0xFFFF = missing */
+  const int64_t* row_offsets;               /* (batch + 1) first node of each row; last = total_nodes */
+  const int32_t* legal_counts;              /* (batch) legal-prefix length of each row */
+  const int64_t* prior_offsets;             /* (batch) sum of legal_counts over the rows before */
+  int batch;
+} sb_payload;
+
+/* The reply, on the device (the caller copies it to the wire bytes). */
+typedef struct {
+  float* values;         /* (batch) decoded value, clamped to [-1, 1] (values_bytes) */
+  float* priors;         /* (sum legal_counts) softmax over each row's legal prefix, row order (priors_bytes) */
+  float* moves_left;     /* (batch) decoded moves-left in [0, 209] (moves_left_bytes), or NULL */
+  float* priors_logits;  /* (sum legal_counts) raw policy logits, same layout (priors_logits_bytes), or NULL */
+  int32_t* status;       /* device status word (SB_DEV_ERR_* bits), or NULL */
+} sb_reply;
+
+/* One forward group: rows [start, end) padded to pad_to cells. */
+typedef struct { int start, end, pad_to; } sb_group;
+
+/* plan_groups (inference.py:201-223) on HOST row offsets: padding-aware
+ * grouping of the size-sorted rows; pad_to = node count of the group's first
+ * row rounded up to `quant` (>= quant); a group stops before the pair ceiling
+ * (rows x (pad_to + 8)^2 > pair_ceiling) or before a row smaller than
+ * pad_to - max(quant, int(waste_fraction * pad_to)). The reference uses
+ * quant 64, waste_fraction 0.18, pair_ceiling 3.8e7. `groups` holds room for
+ * `batch` entries. Rows out of size order are rejected. */
+int sb_plan_groups(const int64_t* row_offsets, int batch, int quant, double waste_fraction, double pair_ceiling,
+                   sb_group* groups, int* num_groups);
+int sb_evaluate_workspace_bytes(const sb_net* net, const sb_group* groups, int num_groups, size_t* bytes);
+/* Every group's forward straight from the CSR payload: the support rows are
+ * unpacked and padded on the device (no host pack), attention skips each
+ * position's dead key and query tiles, and the heads kernel writes the reply
+ * (decoded value, moves-left, legal-prefix priors and logits). */
+int sb_evaluate_payload(const sb_net* net, const sb_payload* payload, const sb_group* groups, int num_groups,
+                        sb_reply* reply, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- index tables (model.py:860-863 gather_idx; model.py:762-792 _build_pair_u8) */
 /* gather_idx_out (B, Npad, 7) int32 row-local: tap 0 = self, taps 1..6 = nbr,
