@@ -518,7 +518,9 @@ def run_forward(args, name, cfg, rank, world, local, device):
                     "d2h_bytes_per_step": int(d2h),
                     "note": "public module call per step; H2D of the next step and D2H of this step on a "
                             "copy stream overlapping the forward; timed over all steps"},
-            "gpu_launches": ShrimpNet.kernel_launches(cfg["trunk_layout"]) * args.steps,
+            "gpu_launches": ShrimpNet.kernel_launches(
+                cfg["trunk_layout"], grid=npad <= 81 and cfg["channels"] % 64 == 0 and cfg["channels"] <= 128)
+            * args.steps,
             "clocks": clocks,
         }
         line.update(extra)

@@ -18,6 +18,7 @@
 #include "aux.cuh"
 #include "gemm.cuh"
 #include "conv_ts.cuh"
+#include "conv_grid.cuh"
 
 namespace sb {
 namespace {
@@ -352,11 +353,51 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
   return check_launch("conv_ts_kernel");
 }
 
+// The grid conv (conv_grid_kernel) for the forward's 7-tap convs with C = Cin
+// = Cout a multiple of 64 (<= 128). `geo.slot_cell` comes from
+// grid_geom_kernel; the kernel returns at once unless *flag == 1. Returns 1
+// when the shape is not eligible.
+template <typename T>
+int launch_conv_grid(GemmArgs a, const GridGeom& geo, const int* flag, cudaStream_t st) {
+  const int C = a.n_total;
+  if (a.taps != 7 || !a.gidx || a.cin != C || C % 64 || C > 128 || geo.npad > kGridMaxCells) return 1;
+  if (a.lda != a.cin || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16) return 1;
+  // Residual convs keep the windowed kernel: its TMA epilogue moves the fp32
+  // stream rows in bulk, where this kernel's slot-ordered rows would need one
+  // scattered row access per thread.
+  if (a.flags & (EPI_RES16 | EPI_OUT32B | EPI_RESID | EPI_LN_B)) return 1;
+  if (geo.npos <= 0) return SB_OK;
+  a.bn = C;
+  a.kpad = round_up(7 * a.cin, kChunkK);
+  a.skip_flag = flag;
+  a.skip_value = 0;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap mw;
+  memset(&mw, 0, sizeof(mw));
+  if (int s = make_tmap(&mw, a.Bw, bf16, a.kpad, C, a.kpad, C)) return s;
+  const bool heavy = (a.flags & (EPI_RESID | EPI_LN_B)) != 0;
+  const int smem = conv_grid_smem_bytes(C);
+  const void* fn = heavy ? reinterpret_cast<const void*>(conv_grid_kernel<T, true>)
+                         : reinterpret_cast<const void*>(conv_grid_kernel<T, false>);
+  if (int s = ensure_smem(fn, smem)) return s;
+  const long long tiles = cdiv((long long)geo.npos * kGridBlock, kBlockM);
+  const long long jobs = cdiv(tiles, 2);
+  const int grid = (int)(jobs < num_sms() ? jobs : num_sms());
+  if (heavy)
+    launch_ex(conv_grid_kernel<T, true>, grid, kGridThreads, smem, st, a, geo, mw);
+  else
+    launch_ex(conv_grid_kernel<T, false>, grid, kGridThreads, smem, st, a, geo, mw);
+  if (sync_debug())
+    fprintf(stderr, "[sb] conv_grid M=%d C=%d npos=%d smem=%d grid=%d flags=%d\n", a.M, C, geo.npos, smem, grid,
+            a.flags);
+  return check_launch("conv_grid_kernel");
+}
+
 // 7-tap conv over whole positions: the windowed kernel when eligible, else
 // the gather-GEMM.
 template <typename T>
 int launch_conv(const GemmArgs& a, int npos, int cells, int xrows, cudaStream_t st) {
-  const int r = launch_conv_ts<T>(a, npos, cells, xrows, st);
+  int r = launch_conv_ts<T>(a, npos, cells, xrows, st);
   if (r != 1) return r;
   return launch_gemm<T>(a, st);
 }
@@ -474,7 +515,7 @@ constexpr size_t hex_conv_workspace_for(size_t rows) {
 }
 
 struct FwdLayout {
-  size_t seq32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, seqlen;
+  size_t seq32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, seqlen, slotcell, gflag;
   size_t pol32, vlog, mllog;  // payload path only: policy and head logits of a group
   size_t total;
 };
@@ -501,6 +542,8 @@ FwdLayout fwd_layout(int C, int B, int npad, bool payload) {
   L.rowmask = take(R * 4);
   L.coords32 = take(Mc * 2 * 4);
   L.seqlen = take((size_t)B * 4);
+  L.slotcell = take((size_t)B * kGridBlock * 2);
+  L.gflag = take(4);
   if (payload) {
     L.pol32 = take(Mc * 4);
     L.vlog = take((size_t)B * kBins * 4);
@@ -558,7 +601,14 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
   float* rowmask = reinterpret_cast<float*>(ws + L.rowmask);
   int32_t* coords32 = reinterpret_cast<int32_t*>(ws + L.coords32);
   int32_t* seqlen = reinterpret_cast<int32_t*>(ws + L.seqlen);
+  int16_t* slotcell = reinterpret_cast<int16_t*>(ws + L.slotcell);
+  int* gflag = reinterpret_cast<int*>(ws + L.gflag);
   int* err = io.err;
+  // Batches that may lie on the radius-4 grid (the module's dense inputs with
+  // at most 81 cells, C a multiple of 64 up to 128) get the grid conv, chosen
+  // on the device by grid_geom_kernel's flag; the windowed conv is launched
+  // beside it for the other outcome.
+  const bool grid_ok = !io.csr && npad <= kGridMaxCells && C % 64 == 0 && C <= 128;
 
   const int S = npad + kNumTok;
   const long long R = (long long)B * S;
@@ -581,10 +631,12 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
       PrepArgs p = *io.dense;
       p.B = B; p.npad = npad; p.S = S;
       p.feat16 = feat16; p.gidx = gidx; p.rowmask = rowmask; p.coords32 = coords32; p.err = err;
+      p.grid_flag = grid_ok ? gflag : nullptr;
       prep_cells_kernel<<<(unsigned)cdiv(work, 256), 256, 0, st>>>(p);
       if (int s = check_launch("prep_cells_kernel")) return s;
     }
   }
+  const GridGeom ggeo{B, npad, S, slotcell};
   PdlScope pdl_scope(true);
   {
     const long long tot = (long long)B * kNumTok * C;
@@ -592,6 +644,24 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
               (const __half*)net->tokens_ln16, B, S, C, seq32, xa16);
     if (int s = check_launch("init_tokens_kernel")) return s;
   }
+  if (grid_ok) {
+    launch_ex(grid_geom_kernel, (unsigned)cdiv(B, 8), 256, 0, st, (const int32_t*)coords32, (const int32_t*)gidx,
+              (const float*)rowmask, B, npad, S, slotcell, gflag);
+    if (int s = check_launch("grid_geom_kernel")) return s;
+  }
+  // a trunk / policy conv: the grid conv and, for batches the flag rejects,
+  // the windowed conv (each returns at once when the flag selects the other)
+  auto conv = [&](GemmArgs g) -> int {
+    if (grid_ok) {
+      const int r = launch_conv_grid<__half>(g, ggeo, gflag, st);
+      if (r != 1) {
+        if (r != SB_OK) return r;
+        g.skip_flag = gflag;
+        g.skip_value = 1;
+      }
+    }
+    return launch_conv<__half>(g, B, npad, S, st);
+  };
 
   const int nb = net->num_blocks;
   int first_attn = -1;
@@ -642,7 +712,7 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
       g1.ln_a_w = w.ln1_w; g1.ln_a_b = w.ln1_b;
       g1.flags = EPI_LN_A | EPI_RELU | EPI_MASK | EPI_OUT16;
       g1.out16 = y16; g1.ld16 = C;
-      if (int s = launch_conv<__half>(g1, B, npad, S, st)) return s;
+      if (int s = conv(g1)) return s;
       GemmArgs g2 = conv_args(y16, w.w2, w.b2);
       g2.ln_a_w = w.ln2_w; g2.ln_a_b = w.ln2_b; g2.gamma = w.gamma;
       g2.flags = EPI_LN_A | EPI_MASK | EPI_RESID | EPI_POST_RELU | EPI_OUT32 | EPI_OUT16;
@@ -652,7 +722,7 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
         g2.flags |= EPI_LN_B;
         g2.ln_b_w = net->attn[na].ln1_w; g2.ln_b_b = net->attn[na].ln1_b;
       }
-      if (int s = launch_conv<__half>(g2, B, npad, S, st)) return s;
+      if (int s = conv(g2)) return s;
     } else {
       const sb_attn_block_weights& w = net->attn[ai];
       // q | k | v projections of LN1(seq) (model.py:448-455)
@@ -702,7 +772,7 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
   {
     GemmArgs g = conv_args(xa16, net->policy_conv_w, net->policy_conv_b);
     g.flags = EPI_HEAD; g.head_w = net->policy_head_w; g.head_b = net->policy_head_b; g.head_out = io.policy;
-    if (int s = launch_conv<__half>(g, B, npad, S, st)) return s;
+    if (int s = conv(g)) return s;
   }
   // value (+ moves-left) heads and decode (model.py:984-1003, losses.py:40-61)
   {

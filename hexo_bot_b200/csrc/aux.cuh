@@ -55,6 +55,7 @@ struct PrepArgs {
   int32_t* gidx;      // (B*npad, 7) absolute seq rows, -1 = missing
   float* rowmask;     // (B*S)
   int32_t* coords32;  // (B*npad, 2)
+  int* grid_flag;     // set to 1 here (grid_geom_kernel clears it), or NULL
   int* err;
 };
 
@@ -83,6 +84,7 @@ __global__ void prep_cells_kernel(const PrepArgs a) {
   pdl_launch_dependents();
   pdl_wait();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i == 0 && a.grid_flag) *a.grid_flag = 1;
   const long long ncell = (long long)a.B * a.npad;
   if (i < ncell) {
     const int b = (int)(i / a.npad);

@@ -69,6 +69,10 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
     conv_ts_kernel(const GemmArgs a, const ConvTsGeom geo, const __grid_constant__ CUtensorMap tmap_x,
                    const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_o16,
                    const __grid_constant__ CUtensorMap tmap_o32, int stages) {
+  if (a.skip_flag) {
+    pdl_wait();
+    if (*reinterpret_cast<const volatile int*>(a.skip_flag) == a.skip_value) return;
+  }
   extern __shared__ uint8_t smem_raw[];
   constexpr int kSets = HEAVY ? 1 : 2;  // A-builder warp sets
   const int tid = threadIdx.x;

@@ -95,6 +95,8 @@ struct GemmArgs {
   const float* head_w;
   const float* head_b;     // [1] (EPI_HEAD)
   float* head_out;
+  const int* skip_flag;    // if set and *skip_flag == skip_value the kernel returns at once
+  int skip_value;          // (a device-side choice between two launched kernels)
   int seq_len;             // rows per position in the seq layout (for EPI_LNB_TOKENS)
   int ntok;
   int* err;                // device status word
@@ -781,6 +783,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                    const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_o16,
                    const __grid_constant__ CUtensorMap tmap_o32, const __grid_constant__ CUtensorMap tmap_o32b,
                    int stages) {
+  if (a.skip_flag) {
+    pdl_wait();
+    if (*reinterpret_cast<const volatile int*>(a.skip_flag) == a.skip_value) return;
+  }
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;

@@ -516,10 +516,16 @@ class ShrimpNet(nn.Module):
         )
 
     @staticmethod
-    def kernel_launches(layout: str) -> int:
-        """Kernels one forward_policy_value call enqueues."""
+    def kernel_launches(layout: str, grid: bool = False) -> int:
+        """Kernels one forward_policy_value call enqueues. With `grid` (dense
+        inputs of at most 81 cells, channels a multiple of 64 up to 128) the
+        geometry check runs and the first conv of every ConvBlock and the
+        policy conv are launched twice, as the grid conv and as the windowed
+        conv, one of which returns at once."""
 
-        return 2 + 1 + 2 * layout.count("C") + 5 * layout.count("A") + 2
+        n_conv = layout.count("C")
+        dual = n_conv + 1 if grid else 0
+        return 2 + (1 if grid else 0) + 1 + 2 * n_conv + 1 + dual + 5 * layout.count("A") + 1
 
 
 __all__ = ["ShrimpNet", "HexNodeConv", "ConvBlock", "AttnBlock", "RelPosAttention", "LayerScale",
