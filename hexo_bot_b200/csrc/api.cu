@@ -358,7 +358,7 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
 // grid_geom_kernel; the kernel returns at once unless *flag == 1. Returns 1
 // when the shape is not eligible.
 template <typename T>
-int launch_conv_grid(GemmArgs a, const GridGeom& geo, const int* flag, cudaStream_t st) {
+int launch_conv_grid(GemmArgs a, const GridGeom& geo, const int* flag, int skip_value, cudaStream_t st) {
   const int C = a.n_total;
   if (a.taps != 7 || !a.gidx || a.cin != C || C % 64 || C > 128 || geo.npad > kGridMaxCells) return 1;
   if (a.lda != a.cin || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16) return 1;
@@ -370,7 +370,7 @@ int launch_conv_grid(GemmArgs a, const GridGeom& geo, const int* flag, cudaStrea
   a.bn = C;
   a.kpad = round_up(7 * a.cin, kChunkK);
   a.skip_flag = flag;
-  a.skip_value = 0;
+  a.skip_value = skip_value;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mw;
   memset(&mw, 0, sizeof(mw));
@@ -605,10 +605,11 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
   int* gflag = reinterpret_cast<int*>(ws + L.gflag);
   int* err = io.err;
   // Batches that may lie on the radius-4 grid (the module's dense inputs with
-  // at most 81 cells, C a multiple of 64 up to 128) get the grid conv, chosen
-  // on the device by grid_geom_kernel's flag; the windowed conv is launched
-  // beside it for the other outcome.
-  const bool grid_ok = !io.csr && npad <= kGridMaxCells && C % 64 == 0 && C <= 128;
+  // at most 81 cells, C a multiple of 64 up to 128, enough positions for the
+  // grid conv to repay its extra launches) get the grid conv, chosen on the
+  // device by grid_geom_kernel's flag; the windowed conv is launched beside it
+  // for the other outcome.
+  const bool grid_ok = !io.csr && npad <= kGridMaxCells && C % 64 == 0 && C <= 128 && B >= kGridMinBatch;
 
   const int S = npad + kNumTok;
   const long long R = (long long)B * S;
@@ -636,7 +637,7 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
       if (int s = check_launch("prep_cells_kernel")) return s;
     }
   }
-  const GridGeom ggeo{B, npad, S, slotcell};
+  const GridGeom ggeo{B, npad, S, kNumTok, slotcell};
   PdlScope pdl_scope(true);
   {
     const long long tot = (long long)B * kNumTok * C;
@@ -653,7 +654,7 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
   // the windowed conv (each returns at once when the flag selects the other)
   auto conv = [&](GemmArgs g) -> int {
     if (grid_ok) {
-      const int r = launch_conv_grid<__half>(g, ggeo, gflag, st);
+      const int r = launch_conv_grid<__half>(g, ggeo, gflag, 0, st);
       if (r != 1) {
         if (r != SB_OK) return r;
         g.skip_flag = gflag;
@@ -970,36 +971,66 @@ int sb_build_pair_u8(const void* coords, int coords_dtype, const void* mask, int
   return check_launch("pair_u8_kernel");
 }
 
+// Extra workspace of the grid conv path of hex_conv (positions of at most 81
+// cells): the slot table and the eligibility flag, after the base pieces.
+size_t hex_conv_grid_extra(int batch, int npad) {
+  return npad <= kGridMaxCells ? (((size_t)batch * kGridBlock * 2 + 255) & ~size_t(255)) + 256 : 0;
+}
+
 int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes) {
   if (!bytes || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "hex_conv workspace: bad args");
-  *bytes = hex_conv_workspace_for((size_t)batch * npad);
+  *bytes = hex_conv_workspace_for((size_t)batch * npad) + hex_conv_grid_extra(batch, npad);
   return SB_OK;
 }
 
+// allow_grid: positions of at most 81 cells whose gather table embeds in the
+// hex grid run on the grid conv (the workspace then holds the slot table);
+// without it only the base workspace is used.
 static int hex_conv_common(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w,
                            const float* bias, const float* ln_w, const float* ln_b, float eps, int flags,
                            int batch, int npad, int cin, int cout, void* out, void* workspace,
-                           size_t workspace_bytes, void* stream) {
+                           size_t workspace_bytes, void* stream, bool allow_grid) {
   if (!x || !gather_idx || !mask || !w || !bias || !out || batch < 0 || npad <= 0)
     return fail(SB_ERR_INVALID_ARG, "hex_conv: bad args");
-  size_t need = 0;
-  sb_hex_conv_workspace_bytes(batch, npad, &need);
-  if (!workspace || workspace_bytes < need) return fail(SB_ERR_WORKSPACE, "hex_conv: workspace too small");
+  const size_t base_need = hex_conv_workspace_for((size_t)batch * npad);
+  const size_t extra = allow_grid ? hex_conv_grid_extra(batch, npad) : 0;
+  if (!workspace || workspace_bytes < base_need + extra)
+    return fail(SB_ERR_WORKSPACE, "hex_conv: workspace too small");
   const long long rows = (long long)batch * npad;
   if (rows == 0) return SB_OK;
   cudaStream_t st = (cudaStream_t)stream;
   int32_t* gabs = reinterpret_cast<int32_t*>(workspace);
   float* rm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
                                       ((rows * 7 * 4 + (long long)kGidxSlack + 255) & ~255LL));
-  absolute_gidx_kernel<<<(unsigned)cdiv(rows * 7, 256), 256, 0, st>>>(gather_idx, batch, npad, 7, gabs);
-  if (int s = check_launch("absolute_gidx_kernel")) return s;
-  mask_to_float_kernel<<<(unsigned)cdiv(rows, 256), 256, 0, st>>>(mask, rows, rm);
-  if (int s = check_launch("mask_to_float_kernel")) return s;
+  const bool grid = extra > 0 && cin == cout && (cout == 64 || cout == 128) && batch >= kGridMinBatch;
+  int16_t* slot = reinterpret_cast<int16_t*>(reinterpret_cast<uint8_t*>(workspace) + base_need);
+  int* gflag = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + base_need + extra - 256);
+  if (grid) {
+    // tables and grid slots in one pass; *gflag = 1 marks an ineligible batch
+    if (cudaMemsetAsync(gflag, 0, sizeof(int), st) != cudaSuccess) return check_launch("flag reset");
+    grid_embed_kernel<<<(unsigned)cdiv(batch, 8), 256, 0, st>>>(gather_idx, mask, batch, npad, gabs, rm, slot, gflag);
+    if (int s = check_launch("grid_embed_kernel")) return s;
+  } else {
+    absolute_gidx_kernel<<<(unsigned)cdiv(rows * 7, 256), 256, 0, st>>>(gather_idx, batch, npad, 7, gabs);
+    if (int s = check_launch("absolute_gidx_kernel")) return s;
+    mask_to_float_kernel<<<(unsigned)cdiv(rows, 256), 256, 0, st>>>(mask, rows, rm);
+    if (int s = check_launch("mask_to_float_kernel")) return s;
+  }
   GemmArgs g{};
   g.A = x; g.lda = cin; g.a_rows = rows; g.cin = cin; g.taps = 7; g.gidx = gabs; g.M = (int)rows;
   g.Bw = w; g.kpad = round_up(7 * cin, kChunkK); g.n_total = cout; g.bn = 0;
   g.bias = bias; g.ln_a_w = ln_w; g.ln_a_b = ln_b; g.eps = eps; g.rowmask = rm;
   g.flags = flags | EPI_MASK | EPI_OUT16; g.out16 = out; g.ld16 = cout;
+  if (grid) {
+    const GridGeom geo{batch, npad, npad, 0, slot};
+    GemmArgs gg = g;
+    const int r = launch_conv_grid<__half>(gg, geo, gflag, 1, st);
+    if (r != 1) {
+      if (r != SB_OK) return r;
+      g.skip_flag = gflag;
+      g.skip_value = 0;
+    }
+  }
   return launch_conv<__half>(g, batch, npad, npad, st);
 }
 
@@ -1007,7 +1038,7 @@ int sb_hex_conv(const void* x, const int32_t* gather_idx, const uint8_t* mask, c
                 int batch, int npad, int cin, int cout, void* out, void* workspace, size_t workspace_bytes,
                 void* stream) {
   return hex_conv_common(x, gather_idx, mask, w, bias, nullptr, nullptr, 0.f, 0, batch, npad, cin, cout, out,
-                         workspace, workspace_bytes, stream);
+                         workspace, workspace_bytes, stream, true);
 }
 
 // ---- allocation-free hex_conv --------------------------------------------------
@@ -1025,8 +1056,7 @@ static __device__ __align__(256) uint8_t g_hex_conv_scratch[kNoAllocScratchBytes
 int sb_hex_conv_noalloc(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w,
                         const float* bias, int batch, int npad, int cin, int cout, void* out, void* stream) {
   if (batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "hex_conv_noalloc: bad args");
-  size_t need = 0;
-  sb_hex_conv_workspace_bytes(batch, npad, &need);
+  const size_t need = hex_conv_workspace_for((size_t)batch * npad);  // no grid path here
   if (need > kNoAllocScratchBytes)
     return fail(SB_ERR_UNSUPPORTED,
                 "hex_conv_noalloc: batch*npad=%lld rows need %zu scratch bytes; the fixed scratch holds %zu "
@@ -1049,7 +1079,7 @@ int sb_hex_conv_noalloc(const void* x, const int32_t* gather_idx, const uint8_t*
     scratch[dev].store(base, std::memory_order_relaxed);
   }
   return hex_conv_common(x, gather_idx, mask, w, bias, nullptr, nullptr, 0.f, 0, batch, npad, cin, cout, out,
-                         base, kNoAllocScratchBytes, stream);
+                         base, kNoAllocScratchBytes, stream, false);
 }
 
 int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w, const float* bias,
@@ -1057,7 +1087,7 @@ int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask
                    void* out, void* workspace, size_t workspace_bytes, void* stream) {
   if (!ln_w || !ln_b) return fail(SB_ERR_INVALID_ARG, "hex_conv_ln: LayerNorm params NULL");
   return hex_conv_common(x, gather_idx, mask, w, bias, ln_w, ln_b, eps, EPI_LN_A | (relu ? EPI_RELU : 0), batch,
-                         npad, cin, cout, out, workspace, workspace_bytes, stream);
+                         npad, cin, cout, out, workspace, workspace_bytes, stream, true);
 }
 
 int sb_attn_pair(const void* q, const void* k, const void* v, const uint8_t* pair, const float* table2,

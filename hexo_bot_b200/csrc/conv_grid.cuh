@@ -49,6 +49,10 @@ constexpr int kGridStages = 4;  // 64 KB of weights in flight
 constexpr int kGridWarps = 14;
 constexpr int kGridThreads = kGridWarps * 32;
 constexpr int kGridMma = 8, kGridWProducer = 9, kGridWin0 = 10;
+// Below this many positions per launch the windowed conv alone runs: the grid
+// conv's extra launches (geometry check, the kernel the flag skips) cost more
+// than it saves when every conv is one or two tiles per SM.
+constexpr int kGridMinBatch = 1024;
 
 __host__ __device__ constexpr int conv_grid_smem_bytes(int c) {
   return 1024 + 2 * (c / 64) * grid_panel_bytes() + kGridStages * c * 128 + kEpiSmemBytes +
@@ -72,7 +76,8 @@ __device__ __forceinline__ int grid_shift(int tap) {
 struct GridGeom {
   int npos;                // positions
   int npad;                // cells per position in the inputs
-  int S;                   // seq rows per position (tokens + cells)
+  int S;                   // rows per position in the activation / output layout
+  int tokoff;              // rows before the cells in each position's block (8 tokens in the forward)
   const int16_t* slot_cell;  // [npos][100] cell of each slot, -1 = empty
 };
 
@@ -227,7 +232,7 @@ __global__ void __launch_bounds__(kGridThreads, 1)
         if (gs >= 0 && gs < nslots) {
           const long long b = gs / kGridBlock;
           const int cell = __ldg(geo.slot_cell + gs);
-          src = cell >= 0 ? (int)(b * geo.S + kNumTok + cell) : -1;
+          src = cell >= 0 ? (int)(b * geo.S + geo.tokoff + cell) : -1;
         }
         win_src[row] = src;
       }
@@ -307,29 +312,38 @@ __global__ void __launch_bounds__(kGridThreads, 1)
     const EpiVecs ev{vecs, vecs + 1024, vecs + 1024 + 256, vecs + 1024 + 512, vecs + 1024 + 768,
                      vecs + 1024 + 1024, vecs + 1024 + 1280};
     const int r_in = quad * 32 + lane;
+    const bool use_mask = ((a.flags & (EPI_MASK | EPI_HEAD)) != 0) && a.rowmask;
     auto slot_of = [&](int t) { return (long long)t * kBlockM + r_in; };
-    auto cell_of = [&](int t) -> int {
+    // output row context of slot row r_in of tile t (cell, row mask), loaded
+    // one job ahead so the latency hides behind the current job
+    struct Pre { int cell; float mk; };
+    auto pre_of = [&](int t) -> Pre {
       const long long gs = slot_of(t);
-      return (t < ntiles && gs < nslots) ? (int)__ldg(geo.slot_cell + gs) : -1;
+      Pre p{-1, 0.f};
+      if (t < ntiles && gs < nslots) {
+        p.cell = __ldg(geo.slot_cell + gs);
+        if (p.cell >= 0)
+          p.mk = use_mask ? __ldg(a.rowmask + (gs / kGridBlock) * geo.S + geo.tokoff + p.cell) : 1.f;
+      }
+      return p;
     };
-    // every cell of an eligible position is live: the row mask is 1
-    auto grid_row = [&](int t, int cell) {
+    auto grid_row = [&](int t, Pre p) {
       EpiRow er;
       const long long b = slot_of(t) / kGridBlock;
-      er.valid = cell >= 0;
-      er.mc = er.valid ? (int)(b * geo.npad + cell) : 0;
-      er.orow = er.valid ? b * geo.S + kNumTok + cell : 0;
-      er.mk = 1.f;
+      er.valid = p.cell >= 0;
+      er.mc = er.valid ? (int)(b * geo.npad + p.cell) : 0;
+      er.orow = er.valid ? b * geo.S + geo.tokoff + p.cell : 0;
+      er.mk = p.mk;
       er.lnb_row = (a.flags & EPI_LN_B) != 0 && !(a.flags & EPI_LNB_TOKENS);
       return er;
     };
     int i = 0;
-    int c0 = cell_of(2 * blockIdx.x), c1 = cell_of(2 * blockIdx.x + 1);
+    Pre c0 = pre_of(2 * blockIdx.x), c1 = pre_of(2 * blockIdx.x + 1);
     for (int job = blockIdx.x; job < njobs; job += gridDim.x, ++i) {
       const int ab = i & 1;
-      const int cur0 = c0, cur1 = c1;
-      c0 = cell_of(2 * (job + gridDim.x));  // next job's rows, in flight during this one
-      c1 = cell_of(2 * (job + gridDim.x) + 1);
+      const Pre cur0 = c0, cur1 = c1;
+      c0 = pre_of(2 * (job + gridDim.x));  // next job's rows, in flight during this one
+      c1 = pre_of(2 * (job + gridDim.x) + 1);
       EpiRow row = grid_row(2 * job, cur0);
       const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (i >> 1) & 1);
       ok = __all_sync(0xffffffffu, got) != 0;
@@ -411,6 +425,115 @@ __global__ void grid_geom_kernel(const int32_t* coords32, const int32_t* gidx, c
   }
   for (int s = lane; s < kGridBlock; s += 32) slot_cell[(long long)b * kGridBlock + s] = good ? owner[s] : -1;
   if (!good && lane == 0) atomicAnd(flag, 0);
+}
+
+// The op-level hex_conv's tables from its row-local gather table (B, npad, 7)
+// (tap 0 = the cell, missing = npad) and u8 mask: absolute gather rows
+// (-1 = missing), the float row mask, and the grid slots, found from the
+// gather table alone (the op has no coordinates): a search places cell 0 at
+// (0, 0) and the neighbour of a placed cell in direction D_k at its offset
+// +D_k, then shifts the placement into the box. A position is eligible when
+// every cell is placed, the placement fits 9 x 9, slots are unique, and every
+// gather row equals the cell at the grid neighbour. One warp per position;
+// an ineligible position sets *flag (zeroed beforehand).
+__global__ void grid_embed_kernel(const int32_t* local, const uint8_t* mask, int B, int npad, int32_t* gabs,
+                                  float* rowmask, int16_t* slot_cell, int* flag) {
+  __shared__ int8_t qs[8][kGridMaxCells], rs[8][kGridMaxCells];
+  __shared__ int16_t owner_s[8][kGridBlock];
+  __shared__ int16_t nb_s[8][kGridMaxCells][6];  // row-local neighbours, -1 = missing
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * 8 + w;
+  if (b >= B) return;
+  int8_t* q = qs[w];
+  int8_t* r = rs[w];
+  int16_t* owner = owner_s[w];
+  int16_t(*nb)[6] = nb_s[w];
+  const int dq[7] = {0, 1, 0, -1, -1, 0, 1}, dr[7] = {0, 0, 1, 1, 0, -1, -1};
+  const long long row0 = (long long)b * npad;
+  // the op's tables: absolute gather rows (missing = -1) and the float row mask
+  for (int i = lane; i < npad * 7; i += 32) {
+    const int v = local[row0 * 7 + i];
+    gabs[row0 * 7 + i] = (v >= 0 && v < npad) ? (int32_t)(row0 + v) : -1;
+  }
+  for (int n = lane; n < npad; n += 32) rowmask[row0 + n] = mask[row0 + n] ? 1.f : 0.f;
+  bool good = npad <= kGridMaxCells;
+  if (good) {
+    // the position's neighbours into shared memory (all loads in flight at once)
+    for (int i = lane; i < npad * 6; i += 32) {
+      const int n = i / 6, k = i - n * 6;
+      const int v = local[(row0 + n) * 7 + 1 + k];
+      const bool self = local[(row0 + n) * 7] == n;
+      nb[n][k] = (int16_t)((v >= 0 && v < npad && self) ? v : (v >= npad || v < 0 ? -1 : -2));
+    }
+    for (int n = lane; n < npad; n += 32) q[n] = r[n] = 127;
+    for (int s = lane; s < kGridBlock; s += 32) owner[s] = -1;
+    __syncwarp();
+    if (lane == 0) q[0] = r[0] = 0;
+    __syncwarp();
+    // placement: grow from cell 0 along the gather table
+    for (int round = 0; round < npad; ++round) {
+      bool changed = false;
+      for (int n = lane; n < npad; n += 32) {
+        const int qn = q[n], rn = r[n];
+        if (qn == 127) continue;
+        for (int k = 1; k < 7; ++k) {
+          const int j = nb[n][k - 1];
+          if (j >= 0 && q[j] == 127) {
+            q[j] = (int8_t)max(-100, min(100, qn + dq[k]));
+            r[j] = (int8_t)max(-100, min(100, rn + dr[k]));
+            changed = true;
+          }
+        }
+      }
+      __syncwarp();
+      if (!__any_sync(0xffffffffu, changed)) break;
+    }
+    int mnq = 127, mxq = -127, mnr = 127, mxr = -127;
+    for (int n = lane; n < npad; n += 32) {
+      if (q[n] == 127) good = false;
+      mnq = min(mnq, (int)q[n]); mxq = max(mxq, (int)q[n]);
+      mnr = min(mnr, (int)r[n]); mxr = max(mxr, (int)r[n]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      mnq = min(mnq, __shfl_xor_sync(0xffffffffu, mnq, o));
+      mxq = max(mxq, __shfl_xor_sync(0xffffffffu, mxq, o));
+      mnr = min(mnr, __shfl_xor_sync(0xffffffffu, mnr, o));
+      mxr = max(mxr, __shfl_xor_sync(0xffffffffu, mxr, o));
+    }
+    good = __all_sync(0xffffffffu, good) && mxq - mnq <= 2 * kGridR && mxr - mnr <= 2 * kGridR;
+    if (good) {
+      for (int n = lane; n < npad; n += 32) {
+        const int s = (q[n] - mnq) * kGridW + (r[n] - mnr);
+        uint32_t* word = reinterpret_cast<uint32_t*>(owner + (s & ~1));
+        const int shiftb = (s & 1) * 16;
+        uint32_t old = *reinterpret_cast<volatile uint32_t*>(word);
+        while (true) {
+          if (((old >> shiftb) & 0xFFFFu) != 0xFFFFu) { good = false; break; }
+          const uint32_t nv = (old & ~(0xFFFFu << shiftb)) | ((uint32_t)n << shiftb);
+          const uint32_t prev = atomicCAS(word, old, nv);
+          if (prev == old) break;
+          old = prev;
+        }
+      }
+      good = __all_sync(0xffffffffu, good);
+      __syncwarp();
+    }
+    if (good) {
+      // every gather row must be the cell at the grid neighbour (missing = empty)
+      for (int n = lane; n < npad; n += 32) {
+        const int s = (q[n] - mnq) * kGridW + (r[n] - mnr);
+        for (int k = 1; k < 7; ++k) {
+          const int t = s + grid_shift(k);
+          const int want = (t >= 0 && t < kGridBlock) ? owner[t] : -1;
+          if (want != nb[n][k - 1]) good = false;
+        }
+      }
+      good = __all_sync(0xffffffffu, good);
+    }
+  }
+  for (int s = lane; s < kGridBlock; s += 32) slot_cell[(long long)b * kGridBlock + s] = good ? owner[s] : -1;
+  if (!good && lane == 0) atomicOr(flag, 1);
 }
 
 }  // namespace sb

@@ -518,7 +518,8 @@ class ShrimpNet(nn.Module):
     @staticmethod
     def kernel_launches(layout: str, grid: bool = False) -> int:
         """Kernels one forward_policy_value call enqueues. With `grid` (dense
-        inputs of at most 81 cells, channels a multiple of 64 up to 128) the
+        inputs of at most 81 cells, channels a multiple of 64 up to 128, at
+        least 1024 positions) the
         geometry check runs and the first conv of every ConvBlock and the
         policy conv are launched twice, as the grid conv and as the windowed
         conv, one of which returns at once."""

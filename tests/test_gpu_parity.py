@@ -178,12 +178,14 @@ def permute_cells(batch, seed):
     return out, torch.stack(perms)
 
 
-def test_forward_is_equivariant_under_cell_order():
+@pytest.mark.parametrize("copies", [1, 11])
+def test_forward_is_equivariant_under_cell_order(copies):
     """Cells in another order give the same per-cell policy logits and the same
     value: the geometry-cached attention maps every position onto one canonical
-    cell order, so its cache must not depend on the order the rows arrive in."""
+    cell order, so its cache must not depend on the order the rows arrive in,
+    and the grid conv (batches of 1024+ positions) places cells by coordinates."""
     model, _ = build(MAIN, 4, True)
-    batch = P.disk_batch(96, 5, 60, 4)
+    batch = P.tile_batch(P.disk_batch(96, 5, 60, 4), copies)
     shuffled, perms = permute_cells(batch, 11)
     a = run(model, batch)
     b = run(model, shuffled)
@@ -400,3 +402,44 @@ def test_programmatic_dependent_launch_gives_identical_results(tmp_path):
         outs.append(torch.load(path))
     for k in outs[0]:
         assert torch.equal(outs[0][k], outs[1][k]), k
+
+
+@pytest.mark.parametrize("cin", [64, 128])
+def test_hex_conv_ops_on_hex_grid_positions(cin):
+    """Disk-regime gather tables (the cells of each position form a piece of
+    the hex lattice) at 1040 positions: sb_hex_conv / sb_hex_conv_ln take the
+    grid conv, whose neighbour gather is a row offset of the tensor-core
+    operand. Checked against fp32 with cells in their support order, in a
+    shuffled order, and with one position whose table is not a lattice piece
+    (the batch then falls back to the windowed conv)."""
+    base = P.tile_batch(P.disk_batch(40, 6, 60, 4), 26)
+    broken = {k: v.clone() for k, v in base.items()}
+    broken["nbr"][17, :, :] = torch.roll(broken["nbr"][17, :, :], 1, dims=0)
+    for batch in (base, permute_cells(base, 3)[0], broken):
+        b, n = batch["mask"].shape
+        torch.manual_seed(cin)
+        x = torch.randn(b, n, cin, device=DEV).half()
+        nbr = batch["nbr"].to(DEV)
+        gidx = torch.cat([torch.arange(n, device=DEV).view(1, n, 1).expand(b, -1, -1), nbr], 2).int().contiguous()
+        mask = batch["mask"].to(DEV).to(torch.uint8)
+        w = torch.randn(7, cin, cin, device=DEV) / math.sqrt(7 * cin)
+        bias = torch.randn(cin, device=DEV) * 0.1
+        wp = _pack_conv(w)
+        out = torch.full((b, n, cin), float("nan"), dtype=torch.float16, device=DEV)
+        nb = C.c_size_t()
+        lib = _lib.lib()
+        lib.sb_hex_conv_workspace_bytes(b, n, C.byref(nb))
+        ws = torch.empty(nb.value, dtype=torch.uint8, device=DEV)
+        _lib.check(lib.sb_hex_conv(x.data_ptr(), gidx.data_ptr(), mask.data_ptr(), wp.data_ptr(), bias.data_ptr(), b,
+                                   n, cin, cin, out.data_ptr(), ws.data_ptr(), nb.value, stream()), "hex_conv")
+        conv = O.hex_conv(x.float().cpu(), gidx.long().cpu(), mask.bool().cpu(), w.half().float().cpu(), bias.cpu())
+        torch.cuda.synchronize()
+        assert (out.float().cpu() - conv).abs().max().item() <= 1e-2
+        lw = torch.rand(cin, device=DEV) + 0.5
+        lb = torch.randn(cin, device=DEV) * 0.1
+        _lib.check(lib.sb_hex_conv_ln(x.data_ptr(), gidx.data_ptr(), mask.data_ptr(), wp.data_ptr(), bias.data_ptr(),
+                                      lw.data_ptr(), lb.data_ptr(), 1e-5, 1, b, n, cin, cin, out.data_ptr(),
+                                      ws.data_ptr(), nb.value, stream()), "hex_conv_ln")
+        ref = F.relu(F.layer_norm(conv, (cin,), lw.cpu(), lb.cpu(), 1e-5)) * mask.bool().cpu().unsqueeze(-1)
+        torch.cuda.synchronize()
+        assert (out.float().cpu() - ref).abs().max().item() <= 1e-2
