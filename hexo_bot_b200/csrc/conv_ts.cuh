@@ -176,12 +176,12 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
   } else if (warp == kConvWProducer) {
     // ------------------------------------------------------------ weight producer
     if (lane == 0) {
-      uint32_t it = 0;
+      int s = 0;
+      uint32_t ph = 0;  // ring slot and its phase, advanced per stage (no division)
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-        for (int q = 0; q < nst; ++q, ++it) {
-          const int s = it % S;
+        for (int q = 0; q < nst; ++q) {
           const int nc = min(kConvStageChunks, nk - q * kConvStageChunks);
-          if (ok && !mbar_wait_sleep(empty_bar + 8 * s, ((it / S) & 1) ^ 1)) {
+          if (ok && !mbar_wait_sleep(empty_bar + 8 * s, ph ^ 1)) {
             ok = false;
             if (a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
           }
@@ -190,6 +190,10 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
           for (int h = 0; h < nc; ++h)
             tma_load_2d(base + s * stage_bytes + h * chunk_bytes, &tmap_w, (q * kConvStageChunks + h) * kChunkK, 0,
                         full_bar + 8 * s);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
         }
         if (!ok) break;
       }
@@ -204,6 +208,8 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
     const int row = quad * 32 + lane; // row within the tile
     const uint32_t tlane = tmem_base + ((uint32_t)(quad * 32) << 16);
     uint32_t ac = 0;                  // A chunks produced
+    int bslot = 0;                    // ring slot of the next stage and its phase (advanced per stage)
+    uint32_t bph = 0;
     int j = 0;
     // this thread's 7 tap rows for tile t (window-local, -1 = zero)
     const int rp = row / lpb, ri = row - rp * lpb;  // position in the tile, cell in the position
@@ -283,9 +289,12 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
         // completed.
         gather(0, va);
         for (int q = 0; q < nst; ++q) {
-          const uint32_t ai = ac + q;
-          const int slot = ai % S;
-          const bool free_ok = mbar_wait(empty_bar + 8 * slot, ((ai / S) & 1) ^ 1);
+          const int slot = bslot;
+          const bool free_ok = mbar_wait(empty_bar + 8 * slot, bph ^ 1);
+          if (++bslot == S) {
+            bslot = 0;
+            bph ^= 1;
+          }
           ok = __all_sync(0xffffffffu, free_ok) != 0;
           if (!ok) {
             if (lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_PRODUCER);
@@ -309,9 +318,12 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
         // Two sets: set bs stores chunk bs of each stage; the gather of its
         // chunk of the next stage overlaps the store of the current one.
         auto step = [&](int q, uint32_t (&cur)[32], uint32_t (&nxt)[32]) -> bool {
-          const uint32_t ai = ac + q;
-          const int slot = ai % S;
-          const bool free_ok = mbar_wait(empty_bar + 8 * slot, ((ai / S) & 1) ^ 1);
+          const int slot = bslot;
+          const bool free_ok = mbar_wait(empty_bar + 8 * slot, bph ^ 1);
+          if (++bslot == S) {
+            bslot = 0;
+            bph ^= 1;
+          }
           if (!__all_sync(0xffffffffu, free_ok)) return false;
           tc_fence_after();
           const int c = q * kConvStageChunks + bs;
@@ -344,7 +356,10 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
       const uint64_t bdesc0 = sw128_desc(base);
       const uint64_t stage_step = stage_bytes >> 4;
       const uint64_t chunk_step = chunk_bytes >> 4;
-      uint32_t it = 0;
+      // The issuing thread's instruction stream bounds the MMA rate at N <= 128:
+      // ring slot and phase advance by compare (no division), descriptors by adds.
+      int s = 0;
+      uint32_t ph = 0;
       int j = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
         const int ab = j & 1;
@@ -354,25 +369,32 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
         }
         tc_fence_after();
         const uint32_t dacc = tmem_base + ab * acc_cols;
-        for (int q = 0; q < nst; ++q, ++it) {
-          const int s = it % S;
+        for (int q = 0; q < nst; ++q) {
           const int nc = min(kConvStageChunks, nk - q * kConvStageChunks);
-          if (ok && !mbar_wait(full_bar + 8 * s, (it / S) & 1)) {
+          if (ok && !mbar_wait(full_bar + 8 * s, ph)) {
             ok = false;
             if (a.err) atomicOr(a.err, SB_ERRBIT_MMA_FULL);
           }
           tc_fence_after();
           if (ok) {
-            for (int h = 0; h < nc; ++h) {
-              const uint64_t bd = bdesc0 + s * stage_step + h * chunk_step;
-              const uint32_t at = tmem_base + a_col0 + s * (32 * kConvStageChunks) + h * 32;
-              tc_mma_f16_ts(dacc, at, bd, idesc, (q > 0 || h > 0) ? 1u : 0u);
-              tc_mma_f16_ts_acc(dacc, at + 8, bd + 2, idesc);
-              tc_mma_f16_ts_acc(dacc, at + 16, bd + 4, idesc);
-              tc_mma_f16_ts_acc(dacc, at + 24, bd + 6, idesc);
+            const uint64_t bd = bdesc0 + s * stage_step;
+            const uint32_t at = tmem_base + a_col0 + s * (32 * kConvStageChunks);
+            tc_mma_f16_ts(dacc, at, bd, idesc, q > 0 ? 1u : 0u);
+            tc_mma_f16_ts_acc(dacc, at + 8, bd + 2, idesc);
+            tc_mma_f16_ts_acc(dacc, at + 16, bd + 4, idesc);
+            tc_mma_f16_ts_acc(dacc, at + 24, bd + 6, idesc);
+            if (nc > 1) {
+              tc_mma_f16_ts_acc(dacc, at + 32, bd + chunk_step, idesc);
+              tc_mma_f16_ts_acc(dacc, at + 40, bd + chunk_step + 2, idesc);
+              tc_mma_f16_ts_acc(dacc, at + 48, bd + chunk_step + 4, idesc);
+              tc_mma_f16_ts_acc(dacc, at + 56, bd + chunk_step + 6, idesc);
             }
           }
           tc_commit(empty_bar + 8 * s);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
         }
         tc_commit(accf_bar + 8 * ab);
       }
