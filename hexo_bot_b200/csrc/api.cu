@@ -60,25 +60,33 @@ int check_launch(const char* what) {
 
 inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 
-// Programmatic dependent launch inside the forward (SHRIMP_B200_PDL=1): every
-// kernel after the first is launched with the programmatic-serialization
-// attribute, so its CTAs start their prologue (barriers, TMEM, tensor-map
-// prefetch, constant loads, the first weight tiles) while the previous kernel
-// drains; each kernel waits (griddepcontrol) before it touches activations.
-// Off by default: measured on B200 under CUDA-graph replay it lowered the
-// batch-256 latency by ~2 % but cost ~1 % at batch 4096 and ~5 % at batch 16.
-int pdl_enabled() {
-  static int v = -1;
-  if (v < 0) {
+// Programmatic dependent launch inside the forward: every kernel after the
+// first is launched with the programmatic-serialization attribute, so its
+// CTAs start their prologue (barriers, TMEM, tensor-map prefetch, constant
+// loads, the first weight tiles) while the previous kernel drains; each kernel
+// waits (griddepcontrol) before it touches activations. Measured on B200
+// under CUDA-graph replay (main-size net, p50): batch 256 -2.7 %, 384 -6.7 %,
+// 512 -6.2 %, 768 -3.0 %, 1024 -1.5 %, but +6 % at batch 16-64 and +0.6-0.8 %
+// at 2048-4096. So it is on for 256 <= B <= 1024. SHRIMP_B200_PDL=0 / =1
+// forces it off / on for every batch.
+constexpr int kPdlMinBatch = 256;
+constexpr int kPdlMaxBatch = 1024;
+int pdl_setting() {  // -1 automatic, 0 off, 1 on
+  static int v = -2;
+  if (v == -2) {
     const char* e = getenv("SHRIMP_B200_PDL");
-    v = (e && strcmp(e, "1") == 0) ? 1 : 0;
+    v = (e && strcmp(e, "1") == 0) ? 1 : (e && strcmp(e, "0") == 0) ? 0 : -1;
   }
   return v;
+}
+bool pdl_for_batch(int B) {
+  const int v = pdl_setting();
+  return v < 0 ? (B >= kPdlMinBatch && B <= kPdlMaxBatch) : v == 1;
 }
 static thread_local bool t_pdl = false;  // set while the forward schedule is being issued
 struct PdlScope {
   bool prev;
-  explicit PdlScope(bool on) : prev(t_pdl) { t_pdl = on && pdl_enabled(); }
+  explicit PdlScope(bool on) : prev(t_pdl) { t_pdl = on; }
   ~PdlScope() { t_pdl = prev; }
 };
 
@@ -638,7 +646,7 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
     }
   }
   const GridGeom ggeo{B, npad, S, kNumTok, slotcell};
-  PdlScope pdl_scope(true);
+  PdlScope pdl_scope(pdl_for_batch(B));
   {
     const long long tot = (long long)B * kNumTok * C;
     launch_ex(init_tokens_kernel, (unsigned)cdiv(tot, 256), 256, 0, st, net->tokens,

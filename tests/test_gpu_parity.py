@@ -383,9 +383,10 @@ torch.save({k: v.cpu() for k, v in out.items()}, sys.argv[1])
 
 
 def test_programmatic_dependent_launch_gives_identical_results(tmp_path):
-    """SHRIMP_B200_PDL=1 (kernels launched with programmatic stream
-    serialization) changes only launch overlap, never results: the forward of
-    a fresh process with it on is bit-identical to one with it off."""
+    """Programmatic dependent launch (on by default for 256-1024 positions,
+    forced by SHRIMP_B200_PDL=0 / 1) changes only launch overlap, never
+    results: the forward of a fresh process with it forced on is bit-identical
+    to one with it forced off."""
     import os
     import subprocess
     import sys
