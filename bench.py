@@ -520,7 +520,8 @@ def run_forward(args, name, cfg, rank, world, local, device):
                             "copy stream overlapping the forward; timed over all steps"},
             "gpu_launches": ShrimpNet.kernel_launches(
                 cfg["trunk_layout"],
-                grid=npad <= 81 and cfg["channels"] % 64 == 0 and cfg["channels"] <= 128 and shard >= 1024)
+                grid=npad <= 81 and cfg["channels"] % 64 == 0 and cfg["channels"] <= 128 and shard >= 1024,
+                channels=cfg["channels"])
             * args.steps,
             "clocks": clocks,
         }
@@ -724,6 +725,7 @@ def run_serve(args, name, cfg, rank, world, local, device):
     the wire payload in host memory and the reply bytes back, per step."""
 
     from hexo_bot_b200.evaluator import ShrimpEvaluator
+    from hexo_bot_b200.model import ShrimpNet
     from hexo_bot_b200.sharding import shard_range
 
     total = cfg["batch"]
@@ -799,7 +801,9 @@ def run_serve(args, name, cfg, rank, world, local, device):
                     "d2h_bytes_per_step": int(d2h),
                     "note": "ShrimpEvaluator.evaluate_payload per step: host staging, plan_groups, one H2D, the "
                             "group forwards, one D2H and the reply bytes"},
-            "gpu_launches": None,
+            # per group the whole forward: prep_csr, tokens, stem, the trunk, policy conv, heads
+            "gpu_launches": len(groups) * ShrimpNet.kernel_launches(cfg["trunk_layout"], grid=False,
+                                                                    channels=cfg["channels"]) * args.steps,
             "groups": len(groups),
             "nodes": {"min": int(sizes.min()), "p50": int(np.median(sizes)), "max": int(sizes.max())},
             "clocks": clocks,

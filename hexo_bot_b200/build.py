@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 OUT_DIR = PKG / "_native"
 LIB_NAME = "libshrimp_b200.so"
 SOURCES = ["api.cu"]
-HEADERS = ["ptx.cuh", "gemm.cuh", "conv_ts.cuh", "conv_grid.cuh", "attention.cuh", "attention_geo.cuh", "aux.cuh"]
+HEADERS = ["ptx.cuh", "gemm.cuh", "conv_ts.cuh", "conv_grid.cuh", "mlp.cuh", "attention.cuh", "attention_geo.cuh", "aux.cuh"]
 INCLUDE = PKG.parent / "include"
 
 NVCC_FLAGS = [

@@ -19,6 +19,7 @@
 #include "gemm.cuh"
 #include "conv_ts.cuh"
 #include "conv_grid.cuh"
+#include "mlp.cuh"
 
 namespace sb {
 namespace {
@@ -281,6 +282,36 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
     fprintf(stderr, "[sb] gemm M=%d N=%d bn=%d kpad=%d taps=%d cin=%d tma=%d tma_epi=%d stages=%d smem=%d grid=%d "
             "flags=%d\n", a.M, a.n_total, a.bn, a.kpad, a.taps, a.cin, a.use_tma, a.tma_epi, stages, smem, grid, a.flags);
   return check_launch("gemm_ws_kernel");
+}
+
+// Fused attention-block MLP (mlp_kernel) for C = 64 or 128 with 16-byte
+// aligned operands; returns 1 when not eligible (the caller then runs fc1 and
+// fc2 as two GEMMs), else an sb_status. w1: [2C][C] and w2: [C][2C] packed
+// K-major 16-bit weights; out32: the fp32 stream (residual, updated in place);
+// out16: the LayerNorm'd 16-bit rows.
+template <typename T>
+int launch_mlp(const MlpArgs& a, const void* w1, const void* w2, float* out32, void* out16, cudaStream_t st) {
+  if (a.M <= 0) return SB_OK;
+  const int C = a.C;
+  if ((C != 64 && C != 128) || (uintptr_t)a.X % 16 || (uintptr_t)w1 % 16 || (uintptr_t)w2 % 16 ||
+      (uintptr_t)out32 % 16 || (uintptr_t)out16 % 16)
+    return 1;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap mx, m1, m2, m16, m32;
+  if (int s = make_tmap(&mx, a.X, bf16, C, a.M, C, kBlockM)) return s;
+  if (int s = make_tmap(&m1, w1, bf16, C, 2 * C, C, 2 * C)) return s;
+  if (int s = make_tmap(&m2, w2, bf16, 2 * C, C, 2 * C, C)) return s;
+  const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (int s = make_tmap_ex(&m16, out16, dt16, 2, C, a.M, C, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return s;
+  if (int s = make_tmap_ex(&m32, out32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, a.M, C, 32, 32,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+    return s;
+  const int smem = mlp_smem_bytes(C);
+  if (int s = ensure_smem(reinterpret_cast<const void*>(mlp_kernel<T>), smem)) return s;
+  const long long tiles = cdiv(a.M, kBlockM);
+  const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  launch_ex(mlp_kernel<T>, grid, kMlpThreads, smem, st, a, mx, m1, m2, m16, m32, out32);
+  return check_launch("mlp_kernel");
 }
 
 // Position-windowed 7-tap conv (conv_ts_kernel) when the shape allows it:
@@ -757,6 +788,24 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
       go.gamma = w.gamma_attn; go.out32 = seq32; go.ld32 = C; go.out16 = y16; go.ld16 = C;
       go.ln_b_w = w.ln2_w; go.ln_b_b = w.ln2_b;
       if (int s = launch_gemm<__half>(go, st)) return s;
+      // fc1 + GELU + fc2 + residual + LN in one kernel when C allows it
+      {
+        MlpArgs mp{};
+        mp.X = y16; mp.M = (int)R; mp.C = C; mp.b1 = w.b1; mp.b2 = w.b2; mp.gamma = w.gamma_mlp;
+        mp.rowmask = rowmask; mp.eps = eps; mp.seq_len = S; mp.ntok = kNumTok; mp.err = err;
+        if (pos == nb - 1) {
+          mp.ln_b_w = net->ln_final_w; mp.ln_b_b = net->ln_final_b;
+        } else {
+          mp.ln_b_w = net->attn[ai + 1].ln1_w; mp.ln_b_b = net->attn[ai + 1].ln1_b;
+          mp.lnb_tokens = next_is_attn ? 0 : 1;
+        }
+        const int r = launch_mlp<__half>(mp, w.w1, w.w2, seq32, xa16, st);
+        if (r != 1) {
+          if (r != SB_OK) return r;
+          ++ai;
+          continue;
+        }
+      }
       // fc1 + GELU
       GemmArgs gf1 = linear_args(y16, C, w.w1, 2 * C, w.b1);
       gf1.flags = EPI_GELU | EPI_OUT16; gf1.out16 = u16; gf1.ld16 = 2 * C;

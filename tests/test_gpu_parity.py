@@ -33,6 +33,9 @@ SMOKE = dict(channels=32, attention_heads=4, trunk_layout="CCA")
 MAIN = dict(channels=128, attention_heads=8, trunk_layout="CCACCACCACCA")
 STRESS = dict(channels=192, attention_heads=12, trunk_layout="CCACCACCACCA")
 DEFAULT = dict(channels=96, attention_heads=4, trunk_layout="CCCACCCACCA")
+# 64 channels: the fused MLP at its narrow width, followed by an attention
+# block (LayerNorm on every row), a conv block (token rows only) and the end
+WIDE64 = dict(channels=64, attention_heads=4, trunk_layout="CAACA")
 
 DEV = torch.device("cuda:0")
 
@@ -116,6 +119,8 @@ def test_forward_matches_reference_golden(name):
         (MAIN, 0, lambda: P.disk_batch(32, 0, 60, 4)),
         (STRESS, 1, lambda: P.disk_batch(6, 1, 120, 8)),
         (DEFAULT, 2, lambda: P.support_batch(6, 2, 20, 8)),
+        (WIDE64, 3, lambda: P.disk_batch(40, 3, 40, 4)),
+        (WIDE64, 4, lambda: P.support_batch(8, 4, 20, 4)),
     ],
 )
 @pytest.mark.parametrize("derandomized", [False, True])

@@ -93,4 +93,6 @@ def test_plugin_builds_model():
 
 
 def test_kernel_launch_count():
-    assert ShrimpNet.kernel_launches("CCACCACCACCA") == 2 + 1 + 16 + 20 + 2
+    assert ShrimpNet.kernel_launches("CCACCACCACCA") == 2 + 1 + 16 + 16 + 2
+    assert ShrimpNet.kernel_launches("CCACCACCACCA", channels=192) == 2 + 1 + 16 + 20 + 2
+    assert ShrimpNet.kernel_launches("CCACCACCACCA", grid=True) == 2 + 1 + 1 + 16 + 9 + 16 + 2
