@@ -184,30 +184,30 @@ __device__ __forceinline__ void stats_merge(float& cnt, float& mean, float& m2, 
   cnt = tot;
 }
 
-// Exact (erf) GELU, x * Phi(x), without erff: Phi(x) = 1 - h (x >= 0) or h
-// (x < 0) with h = 0.5 * exp(-z^2) * R(z), z = min(|x| / sqrt(2), 4), and R a
-// degree-11 polynomial fit of exp(z^2) * erfc(z) on [0, 4] (tests/fit_gelu.py
-// produces the coefficients and checks the error: at most ~8e-7 absolute
-// against 0.5 * x * (1 + erf(x / sqrt(2))) over all float32 x). Straight-line
-// code: 11 FMAs of Horner, one exp2 on the special-function unit, no branch.
+// Exact (erf) GELU without erff: x * Phi(x) = max(x, 0) - |x| * (1 - Phi(|x|)),
+// and 1 - Phi(u) = 0.5 * erfc(u / sqrt(2)) = exp(-u^2 / 2) * q(u) with q a
+// degree-9 polynomial fit on u in [0, 4 sqrt(2)] (u clamped there; the term
+// is below 1e-7 past it). tests/fit_gelu.py produces the coefficients and
+// checks the error: at most ~7e-7 absolute against
+// 0.5 * x * (1 + erf(x / sqrt(2))) over all float32 x. Straight-line code:
+// 9 FMAs of Horner, one exp2 on the special-function unit, a NaN-propagating
+// max (GELU(NaN) = NaN), no branch.
 __device__ __forceinline__ float gelu_erf(float x) {
-  const float za = fminf(fabsf(x) * 0.70710678118654752f, 4.f);
-  float p = -3.415930525e-06f;
-  p = fmaf(p, za, 8.719657761e-05f);
-  p = fmaf(p, za, -9.960989457e-04f);
-  p = fmaf(p, za, 6.759798689e-03f);
-  p = fmaf(p, za, -3.060881219e-02f);
-  p = fmaf(p, za, 9.900606157e-02f);
-  p = fmaf(p, za, -2.411291292e-01f);
-  p = fmaf(p, za, 4.644118264e-01f);
-  p = fmaf(p, za, -7.392278245e-01f);
-  p = fmaf(p, za, 9.974668638e-01f);
-  p = fmaf(p, za, -1.128182360e+00f);
-  p = fmaf(p, za, 9.999974348e-01f);
-  float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(za * (za * -1.4426950408889634f)));
-  const float h = 0.5f * p * e;
-  return x * (x >= 0.f ? 1.f - h : h);
+  const float u = fminf(fabsf(x), 5.656854249492380f);
+  float p = -4.508463653e-06f;
+  p = fmaf(p, u, 9.567350002e-05f);
+  p = fmaf(p, u, -9.027047378e-04f);
+  p = fmaf(p, u, 5.085092341e-03f);
+  p = fmaf(p, u, -1.955406764e-02f);
+  p = fmaf(p, u, 5.619602409e-02f);
+  p = fmaf(p, u, -1.293920372e-01f);
+  p = fmaf(p, u, 2.488136186e-01f);
+  p = fmaf(p, u, -3.987478490e-01f);
+  p = fmaf(p, u, 4.999889998e-01f);
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * (u * -0.72134752044448170f)));
+  asm("max.NaN.f32 %0, %1, 0f00000000;" : "=f"(r) : "f"(x));
+  return fmaf(-(u * p), e, r);
 }
 
 // ---- epilogue ---------------------------------------------------------------

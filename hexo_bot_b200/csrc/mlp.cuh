@@ -275,12 +275,13 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       tc_fence_after();
       if (ok) {
         for (int c = 0; c < H; c += 32) {
-          float v[32];
+          float v[32], bb[32];
           tmem_ld32(trow + c, v);
+          ld_vec<32>(vb1 + c, bb);
           uint32_t u[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            u[i] = MmaTraits<T>::pack(gelu_erf(v[2 * i] + vb1[c + 2 * i]), gelu_erf(v[2 * i + 1] + vb1[c + 2 * i + 1]));
+            u[i] = MmaTraits<T>::pack(gelu_erf(v[2 * i] + bb[2 * i]), gelu_erf(v[2 * i + 1] + bb[2 * i + 1]));
           tmem_st16u(trow + (c >> 1), u);
         }
         tmem_wait_st();
@@ -309,8 +310,13 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
           ok = __all_sync(0xffffffffu, rgot) != 0;
           rphase ^= 1u;
           unstage_row32(e.st32, lane, x);
+          {
+            float bb[32], gg[32];
+            ld_vec<32>(vb2 + c, bb);
+            ld_vec<32>(vgam + c, gg);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = fmaf((v[i] + vb2[c + i]) * mk, vgam[c + i], x[i]);
+            for (int i = 0; i < 32; ++i) v[i] = fmaf((v[i] + bb[i]) * mk, gg[i], x[i]);
+          }
           stats_merge_w<32>(cnt, mean, m2, v);
           tmem_stw<32>(tacc + c, v);  // parked for the LayerNorm pass
           stage_row32(e.st32, lane, v);
@@ -319,11 +325,13 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         const float rstd = rsqrtf(m2 / cnt + a.eps);
         tmem_wait_st();
         for (int c = 0; c < C; c += 32) {
-          float v[32];
+          float v[32], ww[32], bb[32];
           stage_reuse(lane);
           tmem_ld32(tacc + c, v);
+          ld_vec<32>(vlnw + c, ww);
+          ld_vec<32>(vlnb + c, bb);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = lnb_row ? fmaf((v[i] - mean) * rstd, vlnw[c + i], vlnb[c + i]) : v[i];
+          for (int i = 0; i < 32; ++i) v[i] = lnb_row ? fmaf((v[i] - mean) * rstd, ww[i], bb[i]) : v[i];
           stage_row16<T>(e.st16, lane, v);
           stage_flush(e, lane, false, nullptr, true, c, m_first);
         }

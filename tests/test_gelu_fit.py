@@ -1,7 +1,8 @@
-"""The epilogue's erf-GELU polynomial (csrc/gemm.cuh gelu_erf): the committed
-coefficients are the fit that tests/fit_gelu.py produces, and the float32
-evaluation stays within 1e-6 of the exact GELU that the reference's MLP
-applies (F.gelu, packages/shrimp/python/shrimp/model.py:513)."""
+"""The epilogues' erf-GELU polynomial (csrc/gemm.cuh gelu_erf, used by the
+fused MLP and the GEMM epilogue): the committed coefficients are the fit that
+tests/fit_gelu.py produces, and the float32 evaluation stays within 1e-6 of the
+exact GELU that the reference's MLP applies (F.gelu,
+packages/shrimp/python/shrimp/model.py:513)."""
 
 import importlib.util
 import re
@@ -22,7 +23,7 @@ def _fit_module():
 def _kernel_coefficients() -> np.ndarray:
     src = (CSRC / "gemm.cuh").read_text()
     body = src[src.index("float gelu_erf(float x)"):]
-    body = body[: body.index("asm(")]
+    body = body[body.index("float p = "): body.index("asm(")]
     vals = re.findall(r"([-+]?\d\.\d+e[-+]\d+)f", body)
     return np.array([float(v) for v in vals])
 
