@@ -34,6 +34,9 @@ EXPORTED = (
     "sb_hex_conv_noalloc",
     "sb_hex_conv_ln",
     "sb_hex_conv_workspace_bytes",
+    "sb_hex_conv_plan",
+    "sb_hex_conv_planned",
+    "sb_hex_conv_ln_planned",
     "sb_attn_pair",
     "sb_pack_hex_conv_weight",
     "sb_pack_linear_weight",
@@ -139,6 +142,9 @@ def lib() -> C.CDLL:
         "sb_hex_conv_noalloc": ([_P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P], i32),
         "sb_hex_conv_ln": ([_P, _P, _P, _P, _P, _P, _P, f32, i32, i32, i32, i32, i32, _P, _P, sz, _P], i32),
         "sb_hex_conv_workspace_bytes": ([i32, i32, C.POINTER(sz)], i32),
+        "sb_hex_conv_plan": ([_P, _P, i32, i32, _P, sz, C.POINTER(i32), _P], i32),
+        "sb_hex_conv_planned": ([_P, _P, sz, i32, _P, _P, i32, i32, i32, i32, _P, _P], i32),
+        "sb_hex_conv_ln_planned": ([_P, _P, sz, i32, _P, _P, _P, _P, f32, i32, i32, i32, i32, i32, _P, _P], i32),
         "sb_attn_pair": ([_P, _P, _P, _P, _P, _P, i32, i32, i32, i32, _P, _P], i32),
         "sb_pack_hex_conv_weight": ([_P, i32, i32, i32, i32, _P, _P], i32),
         "sb_pack_linear_weight": ([_P, i32, i32, _P, _P], i32),

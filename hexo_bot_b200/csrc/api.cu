@@ -1040,6 +1040,74 @@ int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes) {
   return SB_OK;
 }
 
+// Pieces of a hex_conv workspace (or plan) of `rows` = batch * npad rows:
+// absolute gather rows, fp32 row mask and, when the grid extra is present,
+// the grid slot table and the lattice flag (0 = the cells lie on the hex
+// lattice, 1 = they do not).
+struct HexConvTables {
+  int32_t* gabs;
+  float* rm;
+  int16_t* slot;
+  int* gflag;
+};
+static HexConvTables hex_conv_tables_at(void* ws, long long rows, size_t extra) {
+  const size_t base_need = hex_conv_workspace_for((size_t)rows);
+  HexConvTables t;
+  t.gabs = reinterpret_cast<int32_t*>(ws);
+  t.rm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + ((rows * 7 * 4 + (long long)kGidxSlack + 255) & ~255LL));
+  t.slot = reinterpret_cast<int16_t*>(reinterpret_cast<uint8_t*>(ws) + base_need);
+  t.gflag = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + base_need + extra - 256);
+  return t;
+}
+// Batches whose tables get the grid slots (the grid conv repays its table
+// only from 1024 positions of at most 81 cells on).
+static bool hex_conv_grid_batch(int batch, size_t extra) { return extra > 0 && batch >= kGridMinBatch; }
+
+// Build the tables of a gather table + mask into `ws` (grid: with the slots
+// and the lattice flag, which the device sets).
+static int hex_conv_build_tables(const int32_t* gather_idx, const uint8_t* mask, int batch, int npad,
+                                 const HexConvTables& t, bool grid, cudaStream_t st) {
+  const long long rows = (long long)batch * npad;
+  if (grid) {
+    // tables and grid slots in one pass; *gflag = 1 marks an ineligible batch
+    if (cudaMemsetAsync(t.gflag, 0, sizeof(int), st) != cudaSuccess) return check_launch("flag reset");
+    grid_embed_kernel<<<(unsigned)cdiv(batch, 8), 256, 0, st>>>(gather_idx, mask, batch, npad, t.gabs, t.rm, t.slot,
+                                                                 t.gflag);
+    return check_launch("grid_embed_kernel");
+  }
+  absolute_gidx_kernel<<<(unsigned)cdiv(rows * 7, 256), 256, 0, st>>>(gather_idx, batch, npad, 7, t.gabs);
+  if (int s = check_launch("absolute_gidx_kernel")) return s;
+  mask_to_float_kernel<<<(unsigned)cdiv(rows, 256), 256, 0, st>>>(mask, rows, t.rm);
+  return check_launch("mask_to_float_kernel");
+}
+
+// The conv itself over built tables. grid_mode 0: windowed / gather-GEMM
+// only; 1: the grid conv and the windowed conv both launched, the device flag
+// choosing (each returns at once for the other outcome); 2: the caller knows
+// the cells lie on the lattice: the grid conv alone when the conv shape
+// allows it.
+static int hex_conv_run(const void* x, const HexConvTables& t, const void* w, const float* bias, const float* ln_w,
+                        const float* ln_b, float eps, int flags, int batch, int npad, int cin, int cout, void* out,
+                        int grid_mode, cudaStream_t st) {
+  const long long rows = (long long)batch * npad;
+  GemmArgs g{};
+  g.A = x; g.lda = cin; g.a_rows = rows; g.cin = cin; g.taps = 7; g.gidx = t.gabs; g.M = (int)rows;
+  g.Bw = w; g.kpad = round_up(7 * cin, kChunkK); g.n_total = cout; g.bn = 0;
+  g.bias = bias; g.ln_a_w = ln_w; g.ln_a_b = ln_b; g.eps = eps; g.rowmask = t.rm;
+  g.flags = flags | EPI_MASK | EPI_OUT16; g.out16 = out; g.ld16 = cout;
+  if (grid_mode != 0 && cin == cout && (cout == 64 || cout == 128)) {
+    const GridGeom geo{batch, npad, npad, 0, t.slot};
+    GemmArgs gg = g;
+    const int r = launch_conv_grid<__half>(gg, geo, grid_mode == 1 ? t.gflag : nullptr, 1, st);
+    if (r != 1) {
+      if (r != SB_OK || grid_mode == 2) return r;
+      g.skip_flag = t.gflag;
+      g.skip_value = 0;
+    }
+  }
+  return launch_conv<__half>(g, batch, npad, npad, st);
+}
+
 // allow_grid: positions of at most 81 cells whose gather table embeds in the
 // hex grid run on the grid conv (the workspace then holds the slot table);
 // without it only the base workspace is used.
@@ -1056,39 +1124,10 @@ static int hex_conv_common(const void* x, const int32_t* gather_idx, const uint8
   const long long rows = (long long)batch * npad;
   if (rows == 0) return SB_OK;
   cudaStream_t st = (cudaStream_t)stream;
-  int32_t* gabs = reinterpret_cast<int32_t*>(workspace);
-  float* rm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
-                                      ((rows * 7 * 4 + (long long)kGidxSlack + 255) & ~255LL));
-  const bool grid = extra > 0 && cin == cout && (cout == 64 || cout == 128) && batch >= kGridMinBatch;
-  int16_t* slot = reinterpret_cast<int16_t*>(reinterpret_cast<uint8_t*>(workspace) + base_need);
-  int* gflag = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + base_need + extra - 256);
-  if (grid) {
-    // tables and grid slots in one pass; *gflag = 1 marks an ineligible batch
-    if (cudaMemsetAsync(gflag, 0, sizeof(int), st) != cudaSuccess) return check_launch("flag reset");
-    grid_embed_kernel<<<(unsigned)cdiv(batch, 8), 256, 0, st>>>(gather_idx, mask, batch, npad, gabs, rm, slot, gflag);
-    if (int s = check_launch("grid_embed_kernel")) return s;
-  } else {
-    absolute_gidx_kernel<<<(unsigned)cdiv(rows * 7, 256), 256, 0, st>>>(gather_idx, batch, npad, 7, gabs);
-    if (int s = check_launch("absolute_gidx_kernel")) return s;
-    mask_to_float_kernel<<<(unsigned)cdiv(rows, 256), 256, 0, st>>>(mask, rows, rm);
-    if (int s = check_launch("mask_to_float_kernel")) return s;
-  }
-  GemmArgs g{};
-  g.A = x; g.lda = cin; g.a_rows = rows; g.cin = cin; g.taps = 7; g.gidx = gabs; g.M = (int)rows;
-  g.Bw = w; g.kpad = round_up(7 * cin, kChunkK); g.n_total = cout; g.bn = 0;
-  g.bias = bias; g.ln_a_w = ln_w; g.ln_a_b = ln_b; g.eps = eps; g.rowmask = rm;
-  g.flags = flags | EPI_MASK | EPI_OUT16; g.out16 = out; g.ld16 = cout;
-  if (grid) {
-    const GridGeom geo{batch, npad, npad, 0, slot};
-    GemmArgs gg = g;
-    const int r = launch_conv_grid<__half>(gg, geo, gflag, 1, st);
-    if (r != 1) {
-      if (r != SB_OK) return r;
-      g.skip_flag = gflag;
-      g.skip_value = 0;
-    }
-  }
-  return launch_conv<__half>(g, batch, npad, npad, st);
+  const HexConvTables t = hex_conv_tables_at(workspace, rows, extra);
+  const bool grid = hex_conv_grid_batch(batch, extra) && cin == cout && (cout == 64 || cout == 128);
+  if (int s = hex_conv_build_tables(gather_idx, mask, batch, npad, t, grid, st)) return s;
+  return hex_conv_run(x, t, w, bias, ln_w, ln_b, eps, flags, batch, npad, cin, cout, out, grid ? 1 : 0, st);
 }
 
 int sb_hex_conv(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w, const float* bias,
@@ -1145,6 +1184,61 @@ int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask
   if (!ln_w || !ln_b) return fail(SB_ERR_INVALID_ARG, "hex_conv_ln: LayerNorm params NULL");
   return hex_conv_common(x, gather_idx, mask, w, bias, ln_w, ln_b, eps, EPI_LN_A | (relu ? EPI_RELU : 0), batch,
                          npad, cin, cout, out, workspace, workspace_bytes, stream, true);
+}
+
+// ---- planned hex_conv: the tables of one neighbour table, reused ----------
+int sb_hex_conv_plan(const int32_t* gather_idx, const uint8_t* mask, int batch, int npad, void* plan,
+                     size_t plan_bytes, int* lattice, void* stream) {
+  if (!gather_idx || !mask || !lattice || batch < 0 || npad <= 0) return fail(SB_ERR_INVALID_ARG, "hex_conv_plan: bad args");
+  *lattice = 0;
+  const size_t extra = hex_conv_grid_extra(batch, npad);
+  if (!plan || plan_bytes < hex_conv_workspace_for((size_t)batch * npad) + extra)
+    return fail(SB_ERR_WORKSPACE, "hex_conv_plan: plan buffer too small");
+  const long long rows = (long long)batch * npad;
+  if (rows == 0) return SB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const HexConvTables t = hex_conv_tables_at(plan, rows, extra);
+  const bool grid = hex_conv_grid_batch(batch, extra);
+  if (int s = hex_conv_build_tables(gather_idx, mask, batch, npad, t, grid, st)) return s;
+  if (grid) {
+    int flag = 1;
+    if (cudaMemcpyAsync(&flag, t.gflag, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+      return check_launch("hex_conv_plan: reading the lattice flag");
+    *lattice = flag == 0 ? 1 : 0;
+  }
+  return SB_OK;
+}
+
+static int hex_conv_planned(const void* x, const void* plan, size_t plan_bytes, int lattice, const void* w,
+                            const float* bias, const float* ln_w, const float* ln_b, float eps, int flags, int batch,
+                            int npad, int cin, int cout, void* out, void* stream) {
+  if (!x || !plan || !w || !bias || !out || batch < 0 || npad <= 0)
+    return fail(SB_ERR_INVALID_ARG, "hex_conv_planned: bad args");
+  const size_t extra = hex_conv_grid_extra(batch, npad);
+  if (plan_bytes < hex_conv_workspace_for((size_t)batch * npad) + extra)
+    return fail(SB_ERR_WORKSPACE, "hex_conv_planned: plan buffer too small");
+  if (lattice && !hex_conv_grid_batch(batch, extra))
+    return fail(SB_ERR_INVALID_ARG, "hex_conv_planned: lattice=1 for a batch the plan gave no grid slots");
+  const long long rows = (long long)batch * npad;
+  if (rows == 0) return SB_OK;
+  const HexConvTables t = hex_conv_tables_at(const_cast<void*>(plan), rows, extra);
+  return hex_conv_run(x, t, w, bias, ln_w, ln_b, eps, flags, batch, npad, cin, cout, out, lattice ? 2 : 0,
+                      (cudaStream_t)stream);
+}
+
+int sb_hex_conv_planned(const void* x, const void* plan, size_t plan_bytes, int lattice, const void* w,
+                        const float* bias, int batch, int npad, int cin, int cout, void* out, void* stream) {
+  return hex_conv_planned(x, plan, plan_bytes, lattice, w, bias, nullptr, nullptr, 0.f, 0, batch, npad, cin, cout,
+                          out, stream);
+}
+
+int sb_hex_conv_ln_planned(const void* x, const void* plan, size_t plan_bytes, int lattice, const void* w,
+                           const float* bias, const float* ln_w, const float* ln_b, float eps, int relu, int batch,
+                           int npad, int cin, int cout, void* out, void* stream) {
+  if (!ln_w || !ln_b) return fail(SB_ERR_INVALID_ARG, "hex_conv_ln_planned: LayerNorm params NULL");
+  return hex_conv_planned(x, plan, plan_bytes, lattice, w, bias, ln_w, ln_b, eps, EPI_LN_A | (relu ? EPI_RELU : 0),
+                          batch, npad, cin, cout, out, stream);
 }
 
 int sb_attn_pair(const void* q, const void* k, const void* v, const uint8_t* pair, const float* table2,

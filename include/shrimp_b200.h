@@ -217,8 +217,29 @@ int sb_hex_conv_ln(const void* x, const int32_t* gather_idx, const uint8_t* mask
  * Same results as sb_hex_conv. */
 int sb_hex_conv_noalloc(const void* x, const int32_t* gather_idx, const uint8_t* mask, const void* w_packed,
                         const float* bias, int batch, int npad, int cin, int cout, void* out, void* stream);
-/* Workspace for sb_hex_conv / sb_hex_conv_ln. */
+/* Workspace for sb_hex_conv / sb_hex_conv_ln, and the size of a plan. */
 int sb_hex_conv_workspace_bytes(int batch, int npad, size_t* bytes);
+/* Planned hex_conv for callers that run many convs over one neighbour table
+ * (the reference's trunk calls shrimp::hex_conv / hex_conv_ln once per conv
+ * layer with the same nbr, _triton_conv.py:93-128, 198-239; model.py:346-370).
+ * sb_hex_conv_plan builds the per-table state once into `plan` (as many bytes
+ * as sb_hex_conv_workspace_bytes gives): absolute gather rows, the row mask
+ * and, for batches of >= 1024 positions of <= 81 cells, the hex-grid slots.
+ * For such batches it synchronises `stream` once to read whether the cells
+ * lie on the hex lattice (*lattice = 1; else 0) - make it outside stream
+ * capture. Each planned conv
+ * is then a single kernel launch (the grid conv when lattice = 1 and
+ * cin == cout in {64, 128}, else the windowed conv / gather-GEMM); pass the
+ * `lattice` value the plan returned. Results equal sb_hex_conv /
+ * sb_hex_conv_ln on the same table. The plan stays valid while gather_idx and
+ * mask are unchanged; the planned calls only read it. */
+int sb_hex_conv_plan(const int32_t* gather_idx, const uint8_t* mask, int batch, int npad, void* plan,
+                     size_t plan_bytes, int* lattice, void* stream);
+int sb_hex_conv_planned(const void* x, const void* plan, size_t plan_bytes, int lattice, const void* w_packed,
+                        const float* bias, int batch, int npad, int cin, int cout, void* out, void* stream);
+int sb_hex_conv_ln_planned(const void* x, const void* plan, size_t plan_bytes, int lattice, const void* w_packed,
+                           const float* bias, const float* ln_w, const float* ln_b, float eps, int relu, int batch,
+                           int npad, int cin, int cout, void* out, void* stream);
 /* shrimp::attn_pair (_triton_attn.py:132-171): q, k, v (B, H, S, D) f16 with
  * unit stride on D, pair (B, S, S) uint8, table2 (238, H) f32 (the op rounds it
  * to f16: pass f16-representable values for identical results), seq_lens (B)

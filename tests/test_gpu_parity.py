@@ -449,3 +449,61 @@ def test_hex_conv_ops_on_hex_grid_positions(cin):
         ref = F.relu(F.layer_norm(conv, (cin,), lw.cpu(), lb.cpu(), 1e-5)) * mask.bool().cpu().unsqueeze(-1)
         torch.cuda.synchronize()
         assert (out.float().cpu() - ref).abs().max().item() <= 1e-2
+
+
+@pytest.mark.parametrize("cin,cout,count", [(128, 128, 1040), (64, 64, 1040), (128, 128, 40), (64, 128, 1040)])
+def test_planned_hex_conv_equals_unplanned(cin, cout, count):
+    """sb_hex_conv_plan builds one neighbour table's state once; every planned
+    conv (sb_hex_conv_planned / sb_hex_conv_ln_planned, one kernel each) gives
+    bit-identical outputs to sb_hex_conv / sb_hex_conv_ln, with the plan
+    reused across calls. `lattice` is 1 exactly for grid-sized batches whose
+    cells lie on the hex lattice (in support order or shuffled), 0 for a
+    batch with one broken position and for small batches."""
+    base = P.tile_batch(P.disk_batch(40, 6, 60, 4), count // 40)
+    broken = {k: v.clone() for k, v in base.items()}
+    broken["nbr"][17, :, :] = torch.roll(broken["nbr"][17, :, :], 1, dims=0)
+    lib = _lib.lib()
+    for name, batch in (("base", base), ("shuffled", permute_cells(base, 3)[0]), ("broken", broken)):
+        b, n = batch["mask"].shape
+        torch.manual_seed(cin + cout)
+        nbr = batch["nbr"].to(DEV)
+        gidx = torch.cat([torch.arange(n, device=DEV).view(1, n, 1).expand(b, -1, -1), nbr], 2).int().contiguous()
+        mask = batch["mask"].to(DEV).to(torch.uint8)
+        nb = C.c_size_t()
+        lib.sb_hex_conv_workspace_bytes(b, n, C.byref(nb))
+        plan = torch.empty(nb.value, dtype=torch.uint8, device=DEV)
+        ws = torch.empty(nb.value, dtype=torch.uint8, device=DEV)
+        lattice = C.c_int(-1)
+        _lib.check(lib.sb_hex_conv_plan(gidx.data_ptr(), mask.data_ptr(), b, n, plan.data_ptr(), nb.value,
+                                        C.byref(lattice), stream()), "hex_conv_plan")
+        assert lattice.value == (1 if b >= 1024 and name != "broken" else 0), (name, b, lattice.value)
+        for rep in range(2):
+            x = torch.randn(b, n, cin, device=DEV).half()
+            w = torch.randn(7, cin, cout, device=DEV) / math.sqrt(7 * cin)
+            bias = torch.randn(cout, device=DEV) * 0.1
+            lw = torch.rand(cout, device=DEV) + 0.5
+            lb = torch.randn(cout, device=DEV) * 0.1
+            wp = _pack_conv(w)
+            outs = [torch.full((b, n, cout), float("nan"), dtype=torch.float16, device=DEV) for _ in range(4)]
+            _lib.check(lib.sb_hex_conv(x.data_ptr(), gidx.data_ptr(), mask.data_ptr(), wp.data_ptr(),
+                                       bias.data_ptr(), b, n, cin, cout, outs[0].data_ptr(), ws.data_ptr(),
+                                       nb.value, stream()), "hex_conv")
+            _lib.check(lib.sb_hex_conv_planned(x.data_ptr(), plan.data_ptr(), nb.value, lattice.value, wp.data_ptr(),
+                                               bias.data_ptr(), b, n, cin, cout, outs[1].data_ptr(), stream()),
+                       "hex_conv_planned")
+            _lib.check(lib.sb_hex_conv_ln(x.data_ptr(), gidx.data_ptr(), mask.data_ptr(), wp.data_ptr(),
+                                          bias.data_ptr(), lw.data_ptr(), lb.data_ptr(), 1e-5, 1, b, n, cin, cout,
+                                          outs[2].data_ptr(), ws.data_ptr(), nb.value, stream()), "hex_conv_ln")
+            _lib.check(lib.sb_hex_conv_ln_planned(x.data_ptr(), plan.data_ptr(), nb.value, lattice.value,
+                                                  wp.data_ptr(), bias.data_ptr(), lw.data_ptr(), lb.data_ptr(), 1e-5,
+                                                  1, b, n, cin, cout, outs[3].data_ptr(), stream()),
+                       "hex_conv_ln_planned")
+            torch.cuda.synchronize()
+            assert torch.equal(outs[0], outs[1]), (name, rep)
+            assert torch.equal(outs[2], outs[3]), (name, rep)
+    # a lattice claim for a batch the plan gave no grid slots is refused
+    if count < 1024:
+        with pytest.raises(RuntimeError):
+            _lib.check(lib.sb_hex_conv_planned(x.data_ptr(), plan.data_ptr(), nb.value, 1, wp.data_ptr(),
+                                               bias.data_ptr(), b, n, cin, cout, outs[1].data_ptr(), stream()),
+                       "hex_conv_planned")
