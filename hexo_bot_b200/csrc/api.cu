@@ -284,18 +284,20 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
   return check_launch("gemm_ws_kernel");
 }
 
-// Fused attention-block MLP (mlp_kernel) for C = 64 or 128 with 16-byte
-// aligned operands; returns 1 when not eligible (the caller then runs fc1 and
-// fc2 as two GEMMs), else an sb_status. w1: [2C][C] and w2: [C][2C] packed
-// K-major 16-bit weights; out32: the fp32 stream (residual, updated in place);
-// out16: the LayerNorm'd 16-bit rows.
+// Fused attention-block MLP (mlp_kernel) for C = 64 or 128; returns 1 for
+// other widths (the caller then runs fc1 and fc2 as two GEMMs), else an
+// sb_status (operands must be 16-byte aligned). w1: [2C][C] and w2: [C][2C]
+// packed K-major 16-bit weights; out32: the fp32 stream (residual, updated in
+// place); out16: the LayerNorm'd 16-bit rows.
+inline bool mlp_fused_width(int C) { return C == 64 || C == 128; }
 template <typename T>
 int launch_mlp(const MlpArgs& a, const void* w1, const void* w2, float* out32, void* out16, cudaStream_t st) {
   if (a.M <= 0) return SB_OK;
   const int C = a.C;
-  if ((C != 64 && C != 128) || (uintptr_t)a.X % 16 || (uintptr_t)w1 % 16 || (uintptr_t)w2 % 16 ||
-      (uintptr_t)out32 % 16 || (uintptr_t)out16 % 16)
-    return 1;
+  if (!mlp_fused_width(C)) return 1;
+  if ((uintptr_t)a.X % 16 || (uintptr_t)w1 % 16 || (uintptr_t)w2 % 16 || (uintptr_t)out32 % 16 ||
+      (uintptr_t)out16 % 16)
+    return fail(SB_ERR_INVALID_ARG, "mlp: operands must be 16-byte aligned");
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mx, m1, m2, m16, m32;
   if (int s = make_tmap(&mx, a.X, bf16, C, a.M, C, kBlockM)) return s;
@@ -575,7 +577,8 @@ FwdLayout fwd_layout(int C, int B, int npad, bool payload) {
   L.y16 = take(R * C * 2);
   L.qkv16 = take(R * 3 * C * 2);
   L.o16 = take(R * C * 2);
-  L.u16 = take(R * 2 * C * 2);
+  // the MLP hidden rows: only the unfused fc1 -> fc2 path (C not 64 / 128) keeps them in HBM
+  L.u16 = take(mlp_fused_width(C) ? 0 : R * 2 * C * 2);
   L.feat16 = take(R * kFeatPad * 2);
   L.gidx = take(Mc * 7 * 4 + kGidxSlack);
   L.rowmask = take(R * 4);
