@@ -179,15 +179,15 @@ __global__ void init_tokens_kernel(const float* tokens, const __half* tokens_ln1
                                    float* seq32, __half* xa16) {
   pdl_launch_dependents();
   pdl_wait();
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long total = (long long)B * kNumTok * C;
-  if (i >= total) return;
-  const long long b = i / ((long long)kNumTok * C);
-  const long long r = i - b * kNumTok * C;
-  const long long row = b * S + r / C;
-  const int c = (int)(r % C);
-  seq32[row * C + c] = tokens[r];
-  xa16[row * C + c] = tokens_ln16[r];
+  // one thread per 4 consecutive channels of one token row (C is a multiple of 32)
+  const int per4 = kNumTok * C / 4;  // quads per position
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= B * per4) return;
+  const int b = q / per4;
+  const int r = (q - b * per4) * 4;  // value index within the position's token block
+  const long long o = ((long long)b * S + r / C) * C + r % C;
+  *reinterpret_cast<float4*>(seq32 + o) = __ldg(reinterpret_cast<const float4*>(tokens + r));
+  *reinterpret_cast<uint2*>(xa16 + o) = __ldg(reinterpret_cast<const uint2*>(tokens_ln16 + r));
 }
 
 // gather_idx in the reference's row-local convention (missing -> Npad).
