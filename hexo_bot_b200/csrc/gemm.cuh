@@ -165,18 +165,28 @@ __device__ __forceinline__ void load16_f32(const float* p, float (&v)[16]) {
   }
 }
 
-// Chan's merge of a 16-value chunk into running (count, mean, M2).
+// Chan's merge of a 16-value chunk into running (count, mean, M2). The
+// chunk's sum and squared deviations are formed as balanced trees / four
+// interleaved chains, so the dependent-add latency per chunk is ~6 operations
+// instead of 16.
 __device__ __forceinline__ void stats_merge(float& cnt, float& mean, float& m2, const float (&v)[16]) {
-  float s = 0.f;
+  float t[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) s += v[i];
+  for (int i = 0; i < 8; ++i) t[i] = v[2 * i] + v[2 * i + 1];
+  const float s = ((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7]));
   const float cm = s * (1.f / 16.f);
-  float c2 = 0.f;
+  float q[4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float d = v[i] - cm;
-    c2 = fmaf(d, d, c2);
+  for (int k = 0; k < 4; ++k) {
+    const float d = v[k] - cm;
+    q[k] = d * d;
   }
+#pragma unroll
+  for (int i = 4; i < 16; ++i) {
+    const float d = v[i] - cm;
+    q[i & 3] = fmaf(d, d, q[i & 3]);
+  }
+  const float c2 = (q[0] + q[1]) + (q[2] + q[3]);
   const float tot = cnt + 16.f;
   const float delta = cm - mean;
   mean = fmaf(delta, 16.f / tot, mean);
