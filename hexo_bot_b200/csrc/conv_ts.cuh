@@ -444,20 +444,25 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
       const int ab = j & 1;
       const EpiRow row_next = conv_row(t + gridDim.x);  // loads in flight during this tile
+      // rows of this quadrant: cells [qi0, qi0 + 32) of position t * ppt + qp, i.e. rows
+      // tokoff + qi0 ... of that position's block (the 3D maps clip past its end)
+      const EpiTma etma{&tmap_o16, &tmap_o32, &tmap_o32, gbase + stg_off + warp * 6144,
+                        gbase + stg_off + warp * 6144 + 4096, rload_bar + 8 * warp, t * geo.ppt + qp};
+      // the residual rows of the first chunk are requested before the
+      // accumulator is ready, so they arrive during the wait
+      const bool pre = HEAVY && ok && (a.flags & EPI_RESID);
+      if (pre) epi_request_resid(etma, half * (C >> 1), geo.tokoff + qi0, lane);
       const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (j >> 1) & 1);
       ok = __all_sync(0xffffffffu, got) != 0;
       ok = bar_red_and(bar_id, 64, ok);
       if (!ok && lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_EPILOGUE);
       tc_fence_after();
+      if (!ok && pre) epi_drain_resid(etma, rphase);
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
         if constexpr (HEAVY) {
-          // rows of this quadrant: cells [qi0, qi0 + 32) of position t * ppt + qp, i.e. rows
-          // tokoff + qi0 ... of that position's block (the 3D maps clip past its end)
-          const EpiTma etma{&tmap_o16, &tmap_o32, &tmap_o32, gbase + stg_off + warp * 6144,
-                            gbase + stg_off + warp * 6144 + 4096, rload_bar + 8 * warp, t * geo.ppt + qp};
           epilogue_tile_tma<T, HEAVY>(a, ev, etma, rphase, ok, xch, bar_id, half, row, geo.tokoff + qi0, 0, trow,
-                                      lane);
+                                      lane, pre);
         } else {
           epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, 0, trow, lane);
         }

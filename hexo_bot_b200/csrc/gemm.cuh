@@ -637,10 +637,35 @@ __device__ __forceinline__ void stage_reuse(int lane) {
   __syncwarp();
 }
 
+// Request the fp32 residual chunk [col, col + 32) x rows [m_first, +32) into
+// the warp's fp32 staging once the stores that last read it are done
+// (lane 0 issues; the caller's residual barrier phase is consumed by the
+// matching wait in epilogue_tile_tma or epi_drain_resid).
+__device__ __forceinline__ void epi_request_resid(const EpiTma& e, int col, int m_first, int lane) {
+  if (lane == 0) {
+    bulk_wait_read_all();
+    mbar_arrive_expect_tx(e.rbar, 4096);
+    if (e.z < 0)
+      tma_load_2d(smem_u32(e.st32), e.o32, col, m_first, e.rbar);
+    else
+      tma_load_3d(smem_u32(e.st32), e.o32, col, m_first, e.z, e.rbar);
+  }
+  __syncwarp();
+}
+// Wait (bounded) for a requested residual chunk that no epilogue will read
+// (the tile was abandoned after an error), so no copy lands later.
+__device__ __forceinline__ void epi_drain_resid(const EpiTma& e, uint32_t& rphase) {
+  mbar_wait(e.rbar, rphase);
+  rphase ^= 1u;
+}
+
+// pre: the first residual chunk of this warp (columns [half * bn / 2, +32))
+// was already requested with epi_request_resid.
 template <typename T, bool HEAVY>
 __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const EpiVecs& ev, const EpiTma& e,
                                                   uint32_t& rphase, bool& ok, float4* xch, int bar_id, int half,
-                                                  const EpiRow& r, int m_first, int n0, uint32_t tbase, int lane) {
+                                                  const EpiRow& r, int m_first, int n0, uint32_t tbase, int lane,
+                                                  bool pre = false) {
   const int fl = HEAVY ? a.flags : (a.flags & ~(EPI_RESID | EPI_RES16 | EPI_LN_B));
   const int hw = a.bn >> 1;                     // columns per half (a multiple of 32 here)
   const int c_lo = half * hw, c_hi = c_lo + hw;
@@ -669,13 +694,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const EpiVe
     float v[32], t[32], x[32];
     stage_reuse(lane);
     if (HEAVY && (fl & EPI_RESID)) {
-      if (lane == 0) {
-        mbar_arrive_expect_tx(e.rbar, 4096);
-        if (e.z < 0)
-          tma_load_2d(smem_u32(e.st32), e.o32, n0 + c, m_first, e.rbar);
-        else
-          tma_load_3d(smem_u32(e.st32), e.o32, n0 + c, m_first, e.z, e.rbar);
-      }
+      if (!(pre && c == c_lo)) epi_request_resid(e, n0 + c, m_first, lane);
       const bool got = ok && mbar_wait(e.rbar, rphase);
       ok = __all_sync(0xffffffffu, got) != 0;
       rphase ^= 1u;
@@ -1047,6 +1066,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const EpiRow row_next = make_epi_row(a, (tn / n_tiles) * kBlockM + quad * 32, quad * 32, kBlockM, lane);
       // every lane waits (no lane-dependent control flow ahead of the
       // .sync.aligned TMEM loads of the epilogue)
+      // the residual rows of the first chunk are requested before the
+      // accumulator is ready, so they arrive during the wait
+      const bool pre = TMA_EPI && HEAVY && ok && (a.flags & EPI_RESID);
+      if (pre) epi_request_resid(etma, nt * a.bn + half * (a.bn >> 1), (t / n_tiles) * kBlockM + quad * 32, lane);
       const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (j >> 1) & 1);
       ok = __all_sync(0xffffffffu, got) != 0;
       // Both warps of a quadrant pair must agree on running the tile (they
@@ -1054,11 +1077,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ok = bar_red_and(bar_id, 64, ok);
       if (!ok && lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_EPILOGUE);
       tc_fence_after();
+      if (!ok && pre) epi_drain_resid(etma, rphase);
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
         if constexpr (TMA_EPI)
           epilogue_tile_tma<T, HEAVY>(a, ev, etma, rphase, ok, xch, bar_id, half, row,
-                                      (t / n_tiles) * kBlockM + quad * 32, nt * a.bn, trow, lane);
+                                      (t / n_tiles) * kBlockM + quad * 32, nt * a.bn, trow, lane, pre);
         else
           epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, nt * a.bn, trow, lane);
       }
