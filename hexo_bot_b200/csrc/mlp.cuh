@@ -267,6 +267,9 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       if (lane == 0 && nrows > 0) prefetch_l2_bulk(out32 + (long long)m_first * C, (uint32_t)nrows * C * 4);
       const float mk = __ldg(a.rowmask + mc);
       const bool lnb_row = !a.lnb_tokens || (mc % a.seq_len) < a.ntok;
+      // the first residual chunk lands while the GELU pass and fc2 run
+      const bool pre = ok;
+      if (pre) epi_request_resid(e, 0, m_first, lane);
 
       // ---- GELU pass: fc1 accumulator -> 16-bit h in the same columns
       bool got = ok && mbar_wait_sleep(accf1_bar + 8 * g, k & 1);
@@ -295,16 +298,14 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       ok = __all_sync(0xffffffffu, got) != 0;
       if (!ok && lane == 0 && a.err) atomicOr(a.err, SB_ERRBIT_EPILOGUE);
       tc_fence_after();
+      if (!ok && pre) epi_drain_resid(e, rphase);
       if (ok) {
         const uint32_t tacc = trow + C;
         float cnt = 0.f, mean = 0.f, m2 = 0.f;
         for (int c = 0; c < C; c += 32) {
           float v[32], x[32];
           stage_reuse(lane);
-          if (lane == 0) {
-            mbar_arrive_expect_tx(e.rbar, 4096);
-            tma_load_2d(smem_u32(e.st32), &tmap_o32, c, m_first, e.rbar);
-          }
+          if (c > 0) epi_request_resid(e, c, m_first, lane);
           tmem_ld32(tacc + c, v);
           const bool rgot = ok && mbar_wait(e.rbar, rphase);
           ok = __all_sync(0xffffffffu, rgot) != 0;
