@@ -680,7 +680,7 @@ def run_micro(args, name, cfg, rank, world, local, device):
         launches = 2
         algo = 2.0 * shard * n * taps * c * c
         bound, unit, peak = "tensor", "TFLOP/s", peaks["tflops"]
-        kname = "gemm_ws_kernel (19-tap gather-GEMM, bias + residual + ReLU epilogue)"
+        kname = "conv_ts_kernel<bf16, heavy, 19 taps> (position-windowed ray-tap conv, bias + residual + ReLU epilogue)"
 
     sampler = ClockSampler(local) if rank == 0 else None
     if world > 1:

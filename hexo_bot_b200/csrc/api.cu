@@ -327,9 +327,11 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
   // feature planes: one box of cin columns, K chunks spanning several taps).
   const bool narrow = a.cin == 16 || a.cin == 32;
   // TMEM: two C-column accumulators plus >= 2 A slots of 32 columns in 512.
-  if (a.taps != 7 || !a.gidx || (a.cin != C && !narrow) || C % 64 || 2 * C + 64 > 512 || cells <= 0 ||
-      cells > kBlockM || xrows < cells)
+  // taps: the 7-tap hex conv, or the 19-tap ray conv (16-bit residual epilogue only)
+  if ((a.taps != 7 && a.taps != 19) || !a.gidx || (a.cin != C && !narrow) || C % 64 || 2 * C + 64 > 512 ||
+      cells <= 0 || cells > kBlockM || xrows < cells)
     return 1;
+  if (a.taps == 19 && (narrow || a.flags != (EPI_RES16 | EPI_OUT16))) return 1;
   if (a.lda != a.cin || (uintptr_t)a.A % 16 || (uintptr_t)a.Bw % 16) return 1;
   // positions per tile: 4, 2 or 1 (each position owns 128 / ppt TMEM lanes)
   int ppt = 4;
@@ -345,13 +347,15 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
   const long long conv_tiles = (npos + ppt - 1) / ppt;
   const bool heavy = (a.flags & (EPI_RESID | EPI_RES16 | EPI_LN_B | EPI_OUT32)) != 0 ||
                      ((a.flags & EPI_OUT16) != 0 && conv_tiles > num_sms());
-  if (heavy && (a.flags & (EPI_RES16 | EPI_OUT32B | EPI_HEAD))) return 1;  // not in the TMA epilogue
+  if (heavy && (a.flags & (EPI_OUT32B | EPI_HEAD))) return 1;  // not in the TMA epilogue
+  // the 16-bit residual comes through the fp32 map's slot: not both
+  if ((a.flags & EPI_RES16) && (a.flags & (EPI_RESID | EPI_OUT32 | EPI_LN_B))) return 1;
   const int stages = conv_ts_stages(C, win_rows, heavy);
   const int smem = conv_ts_smem_bytes(C, stages, win_rows, heavy);
   if (smem > 227 * 1024) return 1;
   if (a.M <= 0 || npos <= 0) return SB_OK;
   a.bn = C;
-  a.kpad = round_up(7 * a.cin, kChunkK);
+  a.kpad = round_up(a.taps * a.cin, kChunkK);
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mx, mw;
   memset(&mx, 0, sizeof(mx));
@@ -374,17 +378,27 @@ int launch_conv_ts(GemmArgs a, int npos, int cells, int xrows, cudaStream_t st) 
     const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     if (a.flags & EPI_OUT16)
       if (int s = make_tmap_3d(&m16, a.out16, dt16, 2, C, xrows, npos, a.ld16, CU_TENSOR_MAP_SWIZZLE_64B)) return s;
-    if (int s = make_tmap_3d(&m32, a.out32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, xrows, npos, a.ld32,
-                             CU_TENSOR_MAP_SWIZZLE_128B))
+    if (a.flags & EPI_RES16) {
+      // 16-bit residual rows, staged like the 16-bit outputs
+      if ((uintptr_t)a.res16 % 16 || (a.ldr16 * 2) % 16) return 1;
+      if (int s = make_tmap_3d(&m32, a.res16, dt16, 2, C, xrows, npos, a.ldr16, CU_TENSOR_MAP_SWIZZLE_64B)) return s;
+    } else if (int s = make_tmap_3d(&m32, a.out32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, xrows, npos, a.ld32,
+                                    CU_TENSOR_MAP_SWIZZLE_128B)) {
       return s;
+    }
   }
-  const void* fn = heavy ? reinterpret_cast<const void*>(conv_ts_kernel<T, true>)
-                         : reinterpret_cast<const void*>(conv_ts_kernel<T, false>);
+  const bool ray = a.taps == 19;
+  if (ray && !heavy) return 1;
+  const void* fn = ray     ? reinterpret_cast<const void*>(conv_ts_kernel<T, true, 19>)
+                   : heavy ? reinterpret_cast<const void*>(conv_ts_kernel<T, true>)
+                           : reinterpret_cast<const void*>(conv_ts_kernel<T, false>);
   if (int s = ensure_smem(fn, smem)) return s;
   ConvTsGeom geo{ppt, cells, xrows, npos, xrows - cells};
   const int tiles = (npos + ppt - 1) / ppt;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  if (heavy)
+  if (ray)
+    launch_ex(conv_ts_kernel<T, true, 19>, grid, conv_ts_threads(true), smem, st, a, geo, mx, mw, m16, m32, stages);
+  else if (heavy)
     launch_ex(conv_ts_kernel<T, true>, grid, conv_ts_threads(true), smem, st, a, geo, mx, mw, m16, m32, stages);
   else
     launch_ex(conv_ts_kernel<T, false>, grid, conv_ts_threads(false), smem, st, a, geo, mx, mw, m16, m32, stages);
@@ -1318,6 +1332,10 @@ int sb_raytap_conv(const void* x, const int32_t* nbr, int taps, const void* w, c
   a.A = x; a.lda = c; a.a_rows = (long long)batch * n; a.cin = c; a.taps = taps; a.gidx = g; a.M = batch * n;
   a.Bw = w; a.kpad = round_up(taps * c, kChunkK); a.n_total = c; a.bn = 0;
   a.bias = bias; a.flags = EPI_RES16 | EPI_OUT16; a.res16 = x; a.ldr16 = c; a.out16 = out; a.ld16 = c;
+  // 19 taps on the position-windowed conv (each position's rows loaded once per
+  // tile, the taps gathered on chip), else the gather-GEMM
+  const int r = launch_conv_ts<__nv_bfloat16>(a, batch, n, n, st);
+  if (r != 1) return r;
   return launch_gemm<__nv_bfloat16>(a, st);
 }
 

@@ -1,4 +1,5 @@
-// HexNodeConv (7 taps) for short positions, with the A operand built on chip.
+// HexNodeConv (7 taps; 19 for the ray-tap conv) for short positions, with the
+// A operand built on chip.
 //
 //   out[m, :] = epilogue( sum_t X[src(m, t), :] @ W_t )      (model.py:346-370)
 //
@@ -64,7 +65,7 @@ __host__ __device__ constexpr int conv_ts_stages(int c, int win_rows, bool tma_e
   return s;
 }
 
-template <typename T, bool HEAVY>
+template <typename T, bool HEAVY, int TAPS = 7>
 __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
     conv_ts_kernel(const GemmArgs a, const ConvTsGeom geo, const __grid_constant__ CUtensorMap tmap_x,
                    const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_o16,
@@ -211,26 +212,33 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
     int bslot = 0;                    // ring slot of the next stage and its phase (advanced per stage)
     uint32_t bph = 0;
     int j = 0;
-    // this thread's 7 tap rows for tile t (window-local, -1 = zero)
+    // this thread's TAPS tap rows for tile t (window-local, -1 = zero)
     const int rp = row / lpb, ri = row - rp * lpb;  // position in the tile, cell in the position
-    auto load_src = [&](int t, int (&src)[7]) {
+    auto load_src = [&](int t, int (&src)[TAPS]) {
       const int pos = t * geo.ppt + rp;
       const int m = pos * geo.cells + ri;
       const bool live = ri < geo.cells && pos < geo.npos && m < a.M && t < tiles;
       const int w0 = t * geo.ppt * geo.xrows;
 #pragma unroll
-      for (int k = 0; k < 7; ++k) {
-        int v = live ? __ldg(a.gidx + (long long)m * 7 + k) : -1;
+      for (int k = 0; k < TAPS; ++k) {
+        int v = live ? __ldg(a.gidx + (long long)m * TAPS + k) : -1;
         v = v >= 0 ? v - w0 : -1;
         src[k] = (v >= 0 && v < win_rows) ? v : -1;
       }
     };
-    int src[7], nxt[7];
-    load_src(blockIdx.x, nxt);
+    // 7 taps: the next tile's rows are prefetched during this tile; 19 taps:
+    // loaded at the tile start (two sets of 19 registers would spill)
+    constexpr bool kPrefetch = TAPS <= 7;
+    int src[TAPS], nxt[kPrefetch ? TAPS : 1];
+    if constexpr (kPrefetch) load_src(blockIdx.x, nxt);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+      if constexpr (kPrefetch) {
 #pragma unroll
-      for (int k = 0; k < 7; ++k) src[k] = nxt[k];
-      load_src(t + gridDim.x, nxt);  // prefetch the next tile's rows
+        for (int k = 0; k < TAPS; ++k) src[k] = nxt[k];
+        load_src(t + gridDim.x, nxt);  // prefetch the next tile's rows
+      } else {
+        load_src(t, src);
+      }
       const int wb = j & 1;
       const bool got = ok && mbar_wait_sleep(winf_bar + 8 * wb, (j >> 1) & 1);
       ok = __all_sync(0xffffffffu, got) != 0;
@@ -252,8 +260,8 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
             const int tap = kk / cin;
             int r = src[0];
 #pragma unroll
-            for (int k = 1; k < 7; ++k) r = tap == k ? src[k] : r;
-            r = tap < 7 ? r : -1;
+            for (int k = 1; k < TAPS; ++k) r = tap == k ? src[k] : r;
+            r = tap < TAPS ? r : -1;
             const int rr = r < 0 ? 0 : r;
             const uint32_t keep = r < 0 ? 0u : 0xffffffffu;
             const uint4 u = lds128(win + rr * win_row_bytes + (kk - tap * cin) * 2);
@@ -268,7 +276,7 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
         const int bx = (k0 - tap * C) >> 6;
         int r = src[0];
 #pragma unroll
-        for (int k = 1; k < 7; ++k) r = tap == k ? src[k] : r;  // registers, no local array
+        for (int k = 1; k < TAPS; ++k) r = tap == k ? src[k] : r;  // registers, no local array
         // branch-free: a missing tap reads row 0 and is masked to zero
         const int rr = r < 0 ? 0 : r;
         const uint32_t keep = r < 0 ? 0u : 0xffffffffu;
@@ -430,7 +438,7 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
       const int m = pos * geo.cells + ri;
       er.valid = ri < geo.cells && pos < geo.npos && m < a.M;
       er.mc = er.valid ? m : a.M - 1;
-      er.orow = a.orow_from_gidx ? (long long)__ldg(a.gidx + (long long)er.mc * 7) : (long long)er.mc;
+      er.orow = a.orow_from_gidx ? (long long)__ldg(a.gidx + (long long)er.mc * TAPS) : (long long)er.mc;
       er.mk = ((a.flags & (EPI_MASK | EPI_HEAD)) && a.rowmask) ? __ldg(a.rowmask + er.orow) : 1.f;
       er.lnb_row = (a.flags & EPI_LN_B) != 0;
       if (a.flags & EPI_LNB_TOKENS) er.lnb_row = er.lnb_row && er.valid && (er.orow % a.seq_len) < a.ntok;
@@ -446,8 +454,10 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
       const EpiRow row_next = conv_row(t + gridDim.x);  // loads in flight during this tile
       // rows of this quadrant: cells [qi0, qi0 + 32) of position t * ppt + qp, i.e. rows
       // tokoff + qi0 ... of that position's block (the 3D maps clip past its end)
+      // (a 16-bit residual, EPI_RES16, comes through the map passed in the fp32 slot)
       const EpiTma etma{&tmap_o16, &tmap_o32, &tmap_o32, gbase + stg_off + warp * 6144,
-                        gbase + stg_off + warp * 6144 + 4096, rload_bar + 8 * warp, t * geo.ppt + qp};
+                        gbase + stg_off + warp * 6144 + 4096, rload_bar + 8 * warp, t * geo.ppt + qp,
+                        (a.flags & EPI_RES16) ? &tmap_o32 : nullptr};
       // the residual rows of the first chunk are requested before the
       // accumulator is ready, so they arrive during the wait
       const bool pre = HEAVY && ok && (a.flags & EPI_RESID);
@@ -461,8 +471,8 @@ __global__ void __launch_bounds__(conv_ts_threads(HEAVY), 1)
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
         if constexpr (HEAVY) {
-          epilogue_tile_tma<T, HEAVY>(a, ev, etma, rphase, ok, xch, bar_id, half, row, geo.tokoff + qi0, 0, trow,
-                                      lane, pre);
+          epilogue_tile_tma<T, HEAVY, TAPS == 19>(a, ev, etma, rphase, ok, xch, bar_id, half, row, geo.tokoff + qi0,
+                                                  0, trow, lane, pre);
         } else {
           epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, 0, trow, lane);
         }

@@ -581,6 +581,7 @@ struct EpiTma {
   uint8_t* st16;      // 2 KB, 1024-aligned
   uint32_t rbar;      // residual-load mbarrier of this warp
   int z;              // < 0: 2D maps (col, row); else 3D maps (col, row, z)
+  const CUtensorMap* r16 = nullptr;  // 16-bit residual rows (EPI_RES16), staged through st16
 };
 
 __device__ __forceinline__ void tma_store_box(const EpiTma& e, const CUtensorMap* m, int col, int row, uint32_t src) {
@@ -606,6 +607,16 @@ __device__ __forceinline__ void unstage_row32(const uint8_t* st, int r, float (&
     v[4 * i + 1] = f.y;
     v[4 * i + 2] = f.z;
     v[4 * i + 3] = f.w;
+  }
+}
+template <typename T>
+__device__ __forceinline__ void unstage_row16(const uint8_t* st, int r, float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 u = *reinterpret_cast<const uint4*>(st + st16_addr(r, i));
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[8 * i + e] = to_f32<T>(h[e]);
   }
 }
 template <typename T>
@@ -660,13 +671,16 @@ __device__ __forceinline__ void epi_drain_resid(const EpiTma& e, uint32_t& rphas
 }
 
 // pre: the first residual chunk of this warp (columns [half * bn / 2, +32))
-// was already requested with epi_request_resid.
-template <typename T, bool HEAVY>
+// was already requested with epi_request_resid. R16: the epilogue of the
+// ray-tap conv, v = relu(acc + bias + res16) with the 16-bit residual rows
+// staged through st16 (map e.r16).
+template <typename T, bool HEAVY, bool R16 = false>
 __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const EpiVecs& ev, const EpiTma& e,
                                                   uint32_t& rphase, bool& ok, float4* xch, int bar_id, int half,
                                                   const EpiRow& r, int m_first, int n0, uint32_t tbase, int lane,
                                                   bool pre = false) {
-  const int fl = HEAVY ? a.flags : (a.flags & ~(EPI_RESID | EPI_RES16 | EPI_LN_B));
+  const int fl = R16 ? (a.flags & (EPI_RES16 | EPI_OUT16))
+                     : HEAVY ? a.flags : (a.flags & ~(EPI_RESID | EPI_RES16 | EPI_LN_B));
   const int hw = a.bn >> 1;                     // columns per half (a multiple of 32 here)
   const int c_lo = half * hw, c_hi = c_lo + hw;
   float4* xme = xch + half * 32 + lane;
@@ -700,6 +714,21 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const EpiVe
       rphase ^= 1u;
       unstage_row32(e.st32, lane, x);
     }
+    float x16[32];
+    if (R16) {
+      // the 16-bit residual chunk through the f16 staging (read back in place below)
+      if (lane == 0) {
+        mbar_arrive_expect_tx(e.rbar, 2048);
+        if (e.z < 0)
+          tma_load_2d(smem_u32(e.st16), e.r16, n0 + c, m_first, e.rbar);
+        else
+          tma_load_3d(smem_u32(e.st16), e.r16, n0 + c, m_first, e.z, e.rbar);
+      }
+      const bool got = ok && mbar_wait(e.rbar, rphase);
+      ok = __all_sync(0xffffffffu, got) != 0;
+      rphase ^= 1u;
+      unstage_row16<T>(e.st16, lane, x16);
+    }
     tmem_ld32(tbase + c, v);
     ld_vec<32>(ev.bias + n0 + c, t);
 #pragma unroll
@@ -731,6 +760,10 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const EpiVe
     if (fl & EPI_POST_RELU) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
+    }
+    if (R16) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i] + x16[i], 0.f);
     }
     if (lnb) {
       stats_merge_w<32>(cntb, meanb, m2b, v);
