@@ -863,29 +863,19 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
       h.policy = io.policy; h.npad = npad; h.legal = io.legal; h.prior_offs = io.prior_offs;
       h.priors = io.priors; h.priors_logits = io.priors_logits;
     }
-    // positions per CTA: 4 at small batches; 8 once four per CTA would take
-    // more than two waves; 16 / 32 once eight / sixteen per CTA would take
-    // more than one wave (each CTA streams the layer-1 weights once, so
-    // larger groups re-read them less). A position's outputs do not depend on
-    // the group size.
-    auto fits = [&](int p) { return heads_smem_floats(C, p) * 4 <= 227 * 1024; };
-    int P = 4;
-    if (cdiv(B, 16) > num_sms() && fits(32)) P = 32;
-    else if (cdiv(B, 8) > num_sms() && fits(16)) P = 16;
-    else if (cdiv(B, 4) > 2 * num_sms() && heads_smem_floats(C, 8) * 4 <= 113 * 1024) P = 8;
+    // positions per CTA: 4, or 8 once four per CTA would take more than
+    // two waves (fewer re-reads of the layer-1 weights). Larger groups (16,
+    // 32 per CTA) measured 0.2-1 % slower forwards at B=2048-4096.
+    const int P = (cdiv(B, 4) > 2 * num_sms() && heads_smem_floats(C, 8) * 4 <= 113 * 1024) ? 8 : 4;
     const int smem = heads_smem_floats(C, P) * 4;
-    const void* fn = P == 4    ? reinterpret_cast<const void*>(heads_kernel<4>)
-                     : P == 8  ? reinterpret_cast<const void*>(heads_kernel<8>)
-                     : P == 16 ? reinterpret_cast<const void*>(heads_kernel<16>)
-                               : reinterpret_cast<const void*>(heads_kernel<32>);
+    const void* fn = P == 4 ? reinterpret_cast<const void*>(heads_kernel<4>)
+                            : reinterpret_cast<const void*>(heads_kernel<8>);
     if (int s = ensure_smem(fn, smem)) return s;
     const unsigned grid = (unsigned)cdiv(B, P);
-    switch (P) {
-      case 4: launch_ex(heads_kernel<4>, grid, kHeadsThreads, smem, st, h); break;
-      case 8: launch_ex(heads_kernel<8>, grid, kHeadsThreads, smem, st, h); break;
-      case 16: launch_ex(heads_kernel<16>, grid, kHeadsThreads, smem, st, h); break;
-      default: launch_ex(heads_kernel<32>, grid, kHeadsThreads, smem, st, h);
-    }
+    if (P == 4)
+      launch_ex(heads_kernel<4>, grid, kHeadsThreads, smem, st, h);
+    else
+      launch_ex(heads_kernel<8>, grid, kHeadsThreads, smem, st, h);
     if (int s = check_launch("heads_kernel")) return s;
   }
   return SB_OK;
