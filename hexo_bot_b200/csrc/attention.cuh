@@ -423,7 +423,9 @@ struct AttnStreamSmem {
   static constexpr int kOffLive = kOffCoord + 2 * kStreamBlockK * 8;
   static constexpr int kOffTable = kOffLive + 2 * kStreamBlockK * 4;
   static constexpr int kOffLut = kOffTable + kMaxTableRows * 4;
-  static constexpr int kBytes = kOffLut + kLutW * kLutW + 15;
+  // BIAS_COORDS: the head's bias of every clamped offset, table[lut[dq][dr]] (log2 domain)
+  static constexpr int kOffImg = (kOffLut + kLutW * kLutW + 15) / 16 * 16;
+  static constexpr int kBytes = kOffImg + kLutW * kLutW * 4 + 15;
 };
 
 template <typename T, int DP>
@@ -453,10 +455,19 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
   float* table_s = reinterpret_cast<float*>(smem + SM::kOffTable);
   uint8_t* lut_s = smem + SM::kOffLut;
 
+  float* img_s = reinterpret_cast<float*>(smem + SM::kOffImg);
   for (int i = tid; i < a.table_rows; i += kStreamThreads)
     table_s[i] = __ldg(a.table + (long long)i * a.H + h) * 1.4426950408889634f;  // log2 domain
   if (a.mode == BIAS_COORDS)
     for (int i = tid; i < kLutW * kLutW; i += kStreamThreads) lut_s[i] = __ldg(a.lut + i);
+  __syncthreads();
+  // one lookup per cell pair: the head's bias of each clamped (dq, dr)
+  if (a.mode == BIAS_COORDS)
+    for (int i = tid; i < kLutW * kLutW; i += kStreamThreads) img_s[i] = table_s[min((int)lut_s[i], a.table_rows - 1)];
+  // token rows of model.py:677-716: token->token 236, token->cell 235, cell->token 234
+  const float b_tt = a.mode == BIAS_COORDS ? table_s[min(236, a.table_rows - 1)] : 0.f;
+  const float b_tc = a.mode == BIAS_COORDS ? table_s[min(235, a.table_rows - 1)] : 0.f;
+  const float b_ct = a.mode == BIAS_COORDS ? table_s[min(234, a.table_rows - 1)] : 0.f;
 
   // ---- query fragments (rows q0 + g, q0 + g + 8) ----
   const int q0 = qblk * kStreamBlockQ + warp * 16;
@@ -474,15 +485,17 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
       qa[ks][e] = val;
     }
   }
-  int qq[2] = {0, 0}, qrr[2] = {0, 0};
+  // query coordinates shifted by the clamp radius: a key's image column is
+  // clamp(kq - qq + M, 0, 2M), row clamp(kr - qr + M, 0, 2M)
+  int qq[2] = {kLutM, kLutM}, qrr[2] = {kLutM, kLutM};
   bool qtok[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     qtok[i] = qr[i] < a.ntok;
     if (a.mode == BIAS_COORDS && !qtok[i] && qr[i] < S) {
       const int32_t* c = a.coords + ((long long)b * (S - a.ntok) + (qr[i] - a.ntok)) * 2;
-      qq[i] = __ldg(c);
-      qrr[i] = __ldg(c + 1);
+      qq[i] = __ldg(c) - kLutM;
+      qrr[i] = __ldg(c + 1) - kLutM;
     }
   }
 
@@ -564,27 +577,27 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
         const int key = kb * kStreamBlockK + kloc;
         float val = -INFINITY;
         if (kl[kloc] != 0.f) {
-          int row;
+          float bias;
           if (a.mode == BIAS_COORDS) {
             const bool ktok = key < a.ntok;
             if (qtok[ri]) {
-              row = ktok ? 236 : 235;
+              bias = ktok ? b_tt : b_tc;
             } else if (ktok) {
-              row = 234;
+              bias = b_ct;
             } else {
               const int2 c = kc[kloc];
-              const int dq = min(max(c.x - qq[ri], -kLutM), kLutM);
-              const int dr = min(max(c.y - qrr[ri], -kLutM), kLutM);
-              row = lut_s[(dq + kLutM) * kLutW + dr + kLutM];
+              const int iq = min(max(c.x - qq[ri], 0), 2 * kLutM);
+              const int ir = min(max(c.y - qrr[ri], 0), 2 * kLutM);
+              bias = img_s[iq * kLutW + ir];
             }
           } else if (a.mode == BIAS_PAIR) {
-            row = qr[ri] < S ? __ldg(a.pair + ((long long)b * S + qr[ri]) * S + key) : 0;
-            row = min(row, a.table_rows - 1);
+            int row = qr[ri] < S ? __ldg(a.pair + ((long long)b * S + qr[ri]) * S + key) : 0;
+            bias = table_s[min(row, a.table_rows - 1)];
           } else {
-            row = qr[ri] < S ? __ldg(a.offset_map + (long long)qr[ri] * S + key) : 0;
-            row = min(max(row, 0), a.table_rows - 1);
+            int row = qr[ri] < S ? __ldg(a.offset_map + (long long)qr[ri] * S + key) : 0;
+            bias = table_s[min(max(row, 0), a.table_rows - 1)];
           }
-          val = fmaf(s[j][e], a.scale_log2, table_s[row]);
+          val = fmaf(s[j][e], a.scale_log2, bias);
         }
         s[j][e] = val;
         mx[ri] = fmaxf(mx[ri], val);
@@ -597,7 +610,7 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
       mx[ri] = fmaxf(mx[ri], __shfl_xor_sync(0xffffffffu, mx[ri], 2));
       const float mnew = fmaxf(mrow[ri], mx[ri]);
       const float mref = mnew == -INFINITY ? 0.f : mnew;
-      alpha[ri] = exp2f(mrow[ri] - mref);
+      alpha[ri] = ex2_approx(mrow[ri] - mref);
       mrow[ri] = mnew;
       mx[ri] = mref;
       lrow[ri] *= alpha[ri];
@@ -616,7 +629,7 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
       float p[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        p[e] = exp2f(s[j][e] - mx[e >> 1]);
+        p[e] = ex2_approx(s[j][e] - mx[e >> 1]);
         lrow[e >> 1] += p[e];
       }
       const int i = j >> 1, hi = j & 1;
