@@ -566,8 +566,26 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
         MmaTraits<T>::mma(s[j], qa[ks], kbf);
       }
     }
-    // scale + bias + masks, row maxima
+    // scale + bias + masks, row maxima. A block of live cell keys seen from
+    // cell query rows (the bulk of a long sequence) takes a branch-free path.
     float mx[2] = {-INFINITY, -INFINITY};
+    const bool cells_only = a.mode == BIAS_COORDS && kb * kStreamBlockK >= a.ntok &&
+                            __syncthreads_and(tid >= kStreamBlockK || kl[tid] != 0.f) && q0 >= a.ntok;
+    if (cells_only) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int ri = e >> 1;
+          const int2 c = kc[j * 8 + 2 * t4 + (e & 1)];
+          const int iq = min(max(c.x - qq[ri], 0), 2 * kLutM);
+          const int ir = min(max(c.y - qrr[ri], 0), 2 * kLutM);
+          const float val = fmaf(s[j][e], a.scale_log2, img_s[iq * kLutW + ir]);
+          s[j][e] = val;
+          mx[ri] = fmaxf(mx[ri], val);
+        }
+      }
+    } else {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
 #pragma unroll
@@ -602,6 +620,7 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
         s[j][e] = val;
         mx[ri] = fmaxf(mx[ri], val);
       }
+    }
     }
     float alpha[2];
 #pragma unroll
