@@ -412,6 +412,12 @@ constexpr int kStreamThreads = 128;
 constexpr int kStreamBlockQ = 64;
 constexpr int kStreamBlockK = 64;
 
+// (1.0, 1.0) as a packed pair of T
+template <typename T>
+__device__ __forceinline__ uint32_t one_pair() {
+  return std::is_same<T, __half>::value ? 0x3C003C00u : 0x3F803F80u;
+}
+
 template <int DP>
 struct AttnStreamSmem {
   static constexpr int kRowBytes = DP * 2 + 16;  // padded: conflict-free ldmatrix
@@ -504,7 +510,11 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
   for (int j = 0; j < DP / 8; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
-  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  float mrow[2] = {-INFINITY, -INFINITY};
+  // row sums of P come out of one more MMA per 16 keys, P times a ones tile
+  // (rows g and g + 8 in elements 0 and 2), the same rounded P as the output
+  float osum[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t ones2[2] = {one_pair<T>(), one_pair<T>()};
 
   const int nkb = (n_live + kStreamBlockK - 1) / kStreamBlockK;  // key blocks past the live length: skipped
   const int pieces = DP / 8;  // 16-byte pieces per row (padded)
@@ -632,8 +642,11 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
       alpha[ri] = ex2_approx(mrow[ri] - mref);
       mrow[ri] = mnew;
       mx[ri] = mref;
-      lrow[ri] *= alpha[ri];
     }
+    osum[0] *= alpha[0];
+    osum[1] *= alpha[0];
+    osum[2] *= alpha[1];
+    osum[3] *= alpha[1];
 #pragma unroll
     for (int jd = 0; jd < DP / 8; ++jd) {
       o[jd][0] *= alpha[0];
@@ -647,10 +660,7 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
     for (int j = 0; j < 8; ++j) {
       float p[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        p[e] = ex2_approx(s[j][e] - mx[e >> 1]);
-        lrow[e >> 1] += p[e];
-      }
+      for (int e = 0; e < 4; ++e) p[e] = ex2_approx(s[j][e] - mx[e >> 1]);
       const int i = j >> 1, hi = j & 1;
       pa[i][hi ? 2 : 0] = MmaTraits<T>::pack(p[0], p[1]);
       pa[i][hi ? 3 : 1] = MmaTraits<T>::pack(p[2], p[3]);
@@ -666,17 +676,17 @@ __global__ void __launch_bounds__(kStreamThreads) attn_stream_kernel(const AttnA
         ldmatrix_x2_trans(vb, addr);
         MmaTraits<T>::mma(o[jd], pa[i], vb);
       }
+      MmaTraits<T>::mma(osum, pa[i], ones2);
     }
     __syncthreads();
   }
   cp_async_wait_all();
 
   // normalise and store
+  float lrow[2];
 #pragma unroll
   for (int ri = 0; ri < 2; ++ri) {
-    float l = lrow[ri];
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const float l = osum[2 * ri];
     lrow[ri] = (l > 0.f && qr[ri] < n_live) ? 1.f / l : 0.f;
   }
   T* O = reinterpret_cast<T*>(a.out) + (long long)b * a.out_pos_stride + (long long)h * a.out_head_stride;
