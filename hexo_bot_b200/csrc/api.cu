@@ -965,16 +965,68 @@ int sb_plan_groups(const int64_t* row_offsets, int batch, int quant, double wast
   return SB_OK;
 }
 
-int sb_evaluate_workspace_bytes(const sb_net* net, const sb_group* groups, int num_groups, size_t* bytes) {
-  if (int s = validate_net(net)) return s;
-  if (!bytes || num_groups < 0 || (num_groups > 0 && !groups)) return fail(SB_ERR_INVALID_ARG, "evaluate workspace");
-  size_t need = 0;
+}  // extern "C"
+
+namespace {
+// Serve groups are independent forwards: group i runs on lane i % kServeLanes,
+// lane 0 being the caller's stream and lanes 1.. auxiliary streams of the
+// calling host thread, each lane with its own slice of the workspace. A
+// group's kernels fill only part of the GPU (hundreds of tiles), so the
+// lanes overlap them. Fork and join go through events, which also works
+// while the caller's stream is being captured into a CUDA graph.
+constexpr int kServeLanes = 4;
+
+struct ServeLanes {
+  cudaStream_t aux[kServeLanes - 1] = {};
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join[kServeLanes - 1] = {};
+  bool ready = false;
+};
+
+// Streams and events of this host thread on the current device (created on
+// first use; driver objects, not device memory).
+int serve_lanes(ServeLanes** out) {
+  static thread_local ServeLanes lanes[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(SB_ERR_CUDA, "evaluate: no device");
+  ServeLanes& L = lanes[dev];
+  if (!L.ready) {
+    for (int i = 0; i < kServeLanes - 1; ++i) {
+      if (cudaStreamCreateWithFlags(&L.aux[i], cudaStreamNonBlocking) != cudaSuccess ||
+          cudaEventCreateWithFlags(&L.join[i], cudaEventDisableTiming) != cudaSuccess)
+        return check_launch("evaluate: lane streams");
+    }
+    if (cudaEventCreateWithFlags(&L.fork, cudaEventDisableTiming) != cudaSuccess)
+      return check_launch("evaluate: lane events");
+    L.ready = true;
+  }
+  *out = &L;
+  return SB_OK;
+}
+
+// Workspace slice of each lane: the largest group layout among its groups.
+int serve_lane_bytes(const sb_net* net, const sb_group* groups, int num_groups, size_t (&lane_bytes)[kServeLanes]) {
+  for (int l = 0; l < kServeLanes; ++l) lane_bytes[l] = 0;
   for (int i = 0; i < num_groups; ++i) {
     const int g = groups[i].end - groups[i].start;
     if (g <= 0 || groups[i].pad_to <= 0) return fail(SB_ERR_INVALID_ARG, "evaluate workspace: group %d", i);
-    const size_t t = fwd_layout(net->channels, g, groups[i].pad_to, true).total;
-    need = t > need ? t : need;
+    const size_t t = (fwd_layout(net->channels, g, groups[i].pad_to, true).total + 255) & ~size_t(255);
+    size_t& lb = lane_bytes[i % kServeLanes];
+    lb = t > lb ? t : lb;
   }
+  return SB_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int sb_evaluate_workspace_bytes(const sb_net* net, const sb_group* groups, int num_groups, size_t* bytes) {
+  if (int s = validate_net(net)) return s;
+  if (!bytes || num_groups < 0 || (num_groups > 0 && !groups)) return fail(SB_ERR_INVALID_ARG, "evaluate workspace");
+  size_t lane_bytes[kServeLanes];
+  if (int s = serve_lane_bytes(net, groups, num_groups, lane_bytes)) return s;
+  size_t need = 0;
+  for (int l = 0; l < kServeLanes; ++l) need += lane_bytes[l];
   *bytes = need;
   return SB_OK;
 }
@@ -990,6 +1042,7 @@ int sb_evaluate_payload(const sb_net* net, const sb_payload* payload, const sb_g
     return fail(SB_ERR_INVALID_ARG, "evaluate: NULL payload or reply pointer");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  // validate the whole plan before anything is enqueued
   int covered = 0;
   for (int i = 0; i < num_groups; ++i) {
     const sb_group& gr = groups[i];
@@ -998,19 +1051,46 @@ int sb_evaluate_payload(const sb_net* net, const sb_payload* payload, const sb_g
       return fail(SB_ERR_INVALID_ARG, "evaluate: groups must tile rows 0..%d in order (group %d)", payload->batch, i);
     covered = gr.end;
     if ((long long)g * (gr.pad_to + kNumTok) > (1LL << 31) - 1) return fail(SB_ERR_UNSUPPORTED, "group too large");
+  }
+  if (covered != payload->batch) return fail(SB_ERR_INVALID_ARG, "evaluate: groups cover %d of %d rows", covered,
+                                             payload->batch);
+  size_t lane_bytes[kServeLanes];
+  if (int s = serve_lane_bytes(net, groups, num_groups, lane_bytes)) return s;
+  size_t lane_off[kServeLanes], need = 0;
+  for (int l = 0; l < kServeLanes; ++l) {
+    lane_off[l] = need;
+    need += lane_bytes[l];
+  }
+  if (!workspace || workspace_bytes < need)
+    return fail(SB_ERR_WORKSPACE, "evaluate: workspace %zu < required %zu bytes", workspace_bytes, need);
+  const int nlanes = num_groups < kServeLanes ? num_groups : kServeLanes;
+  ServeLanes* lanes = nullptr;
+  cudaStream_t lane_st[kServeLanes] = {st};
+  if (nlanes > 1) {
+    if (int s = serve_lanes(&lanes)) return s;
+    if (cudaEventRecord(lanes->fork, st) != cudaSuccess) return check_launch("evaluate: fork");
+    for (int l = 1; l < nlanes; ++l) {
+      lane_st[l] = lanes->aux[l - 1];
+      if (cudaStreamWaitEvent(lane_st[l], lanes->fork, 0) != cudaSuccess) return check_launch("evaluate: fork wait");
+    }
+  }
+  int status = SB_OK;
+  for (int i = 0; i < num_groups && status == SB_OK; ++i) {
+    const sb_group& gr = groups[i];
+    const int g = gr.end - gr.start;
+    const int lane = i % kServeLanes;
+    uint8_t* lws = ws + lane_off[lane];
     const FwdLayout L = fwd_layout(net->channels, g, gr.pad_to, true);
-    if (!workspace || workspace_bytes < L.total)
-      return fail(SB_ERR_WORKSPACE, "evaluate: workspace %zu < required %zu bytes", workspace_bytes, L.total);
     PrepCsrArgs p{};
     p.feats = payload->node_feats; p.feats_dtype = payload->feats_dtype;
     p.qr = payload->node_qr; p.nbr = payload->nbr; p.offsets = payload->row_offsets; p.row0 = gr.start;
     FwdIo io{};
     io.csr = &p;
-    io.policy = reinterpret_cast<float*>(ws + L.pol32);
-    io.value_logits = reinterpret_cast<float*>(ws + L.vlog);
+    io.policy = reinterpret_cast<float*>(lws + L.pol32);
+    io.value_logits = reinterpret_cast<float*>(lws + L.vlog);
     io.value = reply->values + gr.start;
     if (reply->moves_left) {
-      io.ml_logits = reinterpret_cast<float*>(ws + L.mllog);
+      io.ml_logits = reinterpret_cast<float*>(lws + L.mllog);
       io.ml = reply->moves_left + gr.start;
     }
     io.legal = payload->legal_counts + gr.start;
@@ -1018,11 +1098,16 @@ int sb_evaluate_payload(const sb_net* net, const sb_payload* payload, const sb_g
     io.priors = reply->priors;
     io.priors_logits = reply->priors_logits;
     io.err = reply->status;
-    if (int s = forward_body(net, g, gr.pad_to, L, ws, io, st)) return s;
+    status = forward_body(net, g, gr.pad_to, L, lws, io, lane_st[lane]);
   }
-  if (covered != payload->batch) return fail(SB_ERR_INVALID_ARG, "evaluate: groups cover %d of %d rows", covered,
-                                             payload->batch);
-  return SB_OK;
+  // join every lane back into the caller's stream (also after an error, so a
+  // capture of the caller's stream is never left with a forked stream)
+  for (int l = 1; l < nlanes; ++l) {
+    if (cudaEventRecord(lanes->join[l - 1], lane_st[l]) != cudaSuccess ||
+        cudaStreamWaitEvent(st, lanes->join[l - 1], 0) != cudaSuccess)
+      return status != SB_OK ? status : check_launch("evaluate: join");
+  }
+  return status;
 }
 
 int sb_build_gather_index(const void* nbr, int nbr_dtype, int batch, int npad, int32_t* out, int32_t* status,

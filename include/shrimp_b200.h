@@ -177,7 +177,13 @@ int sb_evaluate_workspace_bytes(const sb_net* net, const sb_group* groups, int n
 /* Every group's forward straight from the CSR payload: the support rows are
  * unpacked and padded on the device (no host pack), attention skips each
  * position's dead key and query tiles, and the heads kernel writes the reply
- * (decoded value, moves-left, legal-prefix priors and logits). */
+ * (decoded value, moves-left, legal-prefix priors and logits). Groups are
+ * independent and run on up to four lanes: `stream` and three auxiliary
+ * streams of the calling host thread (created on its first call on a device),
+ * forked from and joined back into `stream` by events, so the call is
+ * ordered on `stream` as one unit and may be captured into a CUDA graph.
+ * Each lane has its own slice of the workspace (sb_evaluate_workspace_bytes
+ * sums them). */
 int sb_evaluate_payload(const sb_net* net, const sb_payload* payload, const sb_group* groups, int num_groups,
                         sb_reply* reply, void* workspace, size_t workspace_bytes, void* stream);
 
