@@ -144,3 +144,32 @@ def test_evaluator_rejects_malformed_payloads():
     bad = dict(payload, legal_counts=payload["legal_counts"][:-4])
     with pytest.raises(ValueError, match="legal_counts"):
         ev.evaluate_payload(bad)
+
+
+def test_evaluator_groups_on_lanes_inside_a_cuda_graph():
+    """The groups of a payload run on four stream lanes forked from and joined
+    back into the caller's stream. The whole call captures into one CUDA graph
+    whose replays give the eager reply bit for bit, also after the device
+    reply was overwritten between replays."""
+    model, _ = model_sd(MAIN, 3, True)
+    payload, _ = PL.seeded_payload(40, 11, 60, 4, request_moves_left=True, request_logits=True)
+    ev = ShrimpEvaluator(model, DEV)
+    eager = ev.evaluate_payload(payload)
+    req = ev.stage_payload(payload)
+    assert req["ng"] > 4, req["ng"]  # every lane holds at least one group
+    ev.launch(req)
+    torch.cuda.synchronize()
+    first = req["dev_out"].clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ev.launch(req)
+    for _ in range(2):
+        req["dev_out"].fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(req["dev_out"], first)
+    host = first.cpu().numpy()
+    b, p = req["b"], req["n_priors"]
+    assert host[:b].tobytes() == eager["values_bytes"]
+    assert host[b:b + p].tobytes() == eager["priors_bytes"]
+    assert int(host[-1:].view(np.int32)[0]) == 0
