@@ -244,21 +244,26 @@ int launch_gemm(GemmArgs a, cudaStream_t st) {
   memset(&m16, 0, sizeof(m16));
   memset(&m32, 0, sizeof(m32));
   memset(&m32b, 0, sizeof(m32b));
-  a.tma_epi = a.use_tma && !a.gidx && (a.bn / 2) % 32 == 0 && !(a.flags & (EPI_HEAD | EPI_RES16)) &&
+  // gathered rows qualify when their outputs run contiguously in whole
+  // 32-row quadrants (position blocks of a multiple of 32 rows)
+  const bool rows_contig =
+      !a.gidx || (a.orow_from_gidx && a.orow_run > 0 && a.orow_run % 32 == 0 && a.M % 32 == 0);
+  a.tma_epi = a.use_tma && rows_contig && (a.bn / 2) % 32 == 0 && !(a.flags & (EPI_HEAD | EPI_RES16)) &&
               ((uintptr_t)a.out16 % 16 == 0) && ((uintptr_t)a.out32 % 16 == 0) && ((uintptr_t)a.out32b % 16 == 0) &&
               (a.ld16 * 2) % 16 == 0 && (a.ld32 * 4) % 16 == 0 && (a.ld32b * 4) % 16 == 0;
   if (a.tma_epi) {
     const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const long long orows = a.gidx ? a.a_rows : a.M;  // gathered: outputs share the input's row layout
     if (a.flags & EPI_OUT16)
-      if (int s = make_tmap_ex(&m16, a.out16, dt16, 2, a.n_total, a.M, a.ld16, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      if (int s = make_tmap_ex(&m16, a.out16, dt16, 2, a.n_total, orows, a.ld16, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
         return s;
     if (a.flags & (EPI_OUT32 | EPI_RESID))
-      if (int s = make_tmap_ex(&m32, a.out32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.n_total, a.M, a.ld32, 32, 32,
+      if (int s = make_tmap_ex(&m32, a.out32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.n_total, orows, a.ld32, 32, 32,
                                CU_TENSOR_MAP_SWIZZLE_128B))
         return s;
     if (a.flags & EPI_OUT32B)
-      if (int s = make_tmap_ex(&m32b, a.out32b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.n_total, a.M, a.ld32b, 32, 32,
-                               CU_TENSOR_MAP_SWIZZLE_128B))
+      if (int s = make_tmap_ex(&m32b, a.out32b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.n_total, orows, a.ld32b, 32,
+                               32, CU_TENSOR_MAP_SWIZZLE_128B))
         return s;
   }
   const int stages = gemm_stages(a.bn, a.taps, a.tma_epi);
@@ -454,7 +459,9 @@ template <typename T>
 int launch_conv(const GemmArgs& a, int npos, int cells, int xrows, cudaStream_t st) {
   int r = launch_conv_ts<T>(a, npos, cells, xrows, st);
   if (r != 1) return r;
-  return launch_gemm<T>(a, st);
+  GemmArgs g = a;
+  if (g.orow_from_gidx) g.orow_run = cells;  // each position's cells are consecutive output rows
+  return launch_gemm<T>(g, st);
 }
 
 template <typename T>

@@ -100,7 +100,10 @@ struct GemmArgs {
   int seq_len;             // rows per position in the seq layout (for EPI_LNB_TOKENS)
   int ntok;
   int* err;                // device status word
-  int tma_epi;             // identity rows: epilogue stores / residual loads through TMA (set by the host)
+  int tma_epi;             // epilogue stores / residual loads through TMA (set by the host)
+  int orow_run;            // > 0 with orow_from_gidx: output rows run contiguously in blocks of this
+                           // many GEMM rows (whole positions), so a 32-row quadrant starting at a
+                           // multiple of 32 maps to 32 consecutive output rows
 };
 
 constexpr int kBlockM = 128;
@@ -1099,10 +1102,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const EpiRow row_next = make_epi_row(a, (tn / n_tiles) * kBlockM + quad * 32, quad * 32, kBlockM, lane);
       // every lane waits (no lane-dependent control flow ahead of the
       // .sync.aligned TMEM loads of the epilogue)
+      // this quadrant's first output row for the TMA epilogue: the GEMM row
+      // itself, or (gathered rows in position blocks) its row in the output
+      const int mq = (t / n_tiles) * kBlockM + quad * 32;
+      const bool q_live = !a.gidx || mq < a.M;
+      const int oq = (TMA_EPI && a.gidx && q_live) ? __ldg(a.gidx + (long long)mq * a.taps) : mq;
       // the residual rows of the first chunk are requested before the
       // accumulator is ready, so they arrive during the wait
-      const bool pre = TMA_EPI && HEAVY && ok && (a.flags & EPI_RESID);
-      if (pre) epi_request_resid(etma, nt * a.bn + half * (a.bn >> 1), (t / n_tiles) * kBlockM + quad * 32, lane);
+      const bool pre = TMA_EPI && HEAVY && ok && q_live && (a.flags & EPI_RESID);
+      if (pre) epi_request_resid(etma, nt * a.bn + half * (a.bn >> 1), oq, lane);
       const bool got = ok && mbar_wait_sleep(accf_bar + 8 * ab, (j >> 1) & 1);
       ok = __all_sync(0xffffffffu, got) != 0;
       // Both warps of a quadrant pair must agree on running the tile (they
@@ -1113,9 +1121,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok && pre) epi_drain_resid(etma, rphase);
       if (ok) {
         const uint32_t trow = tmem_base + ab * acc_cols + ((uint32_t)(quad * 32) << 16);
-        if constexpr (TMA_EPI)
-          epilogue_tile_tma<T, HEAVY>(a, ev, etma, rphase, ok, xch, bar_id, half, row,
-                                      (t / n_tiles) * kBlockM + quad * 32, nt * a.bn, trow, lane, pre);
+        if constexpr (TMA_EPI) {
+          if (q_live)  // a gathered quadrant past M has no output rows
+            epilogue_tile_tma<T, HEAVY>(a, ev, etma, rphase, ok, xch, bar_id, half, row, oq, nt * a.bn, trow, lane,
+                                        pre);
+        }
         else
           epilogue_tile<T, HEAVY>(a, ev, xch, bar_id, half, row, nt * a.bn, trow, lane);
       }
