@@ -179,7 +179,8 @@ int sb_evaluate_workspace_bytes(const sb_net* net, const sb_group* groups, int n
  * position's dead key and query tiles, and the heads kernel writes the reply
  * (decoded value, moves-left, legal-prefix priors and logits). Groups are
  * independent and run on up to four lanes: `stream` and three auxiliary
- * streams of the calling host thread (created on its first call on a device),
+ * streams of the calling host thread (created on its first call on a device
+ * and kept for the life of the thread; not recreated after cudaDeviceReset),
  * forked from and joined back into `stream` by events, so the call is
  * ordered on `stream` as one unit and may be captured into a CUDA graph.
  * Each lane has its own slice of the workspace (sb_evaluate_workspace_bytes
