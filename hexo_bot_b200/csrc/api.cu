@@ -517,6 +517,14 @@ int launch_attention(AttnArgs a, cudaStream_t st) {
       if (group) break;
     }
   }
+  // The resident kernel runs one CTA per position. When the batch leaves SM
+  // slots empty and the keys take more than one softmax step, the streaming
+  // kernel's (query block, head, position) grid finishes sooner: this is the
+  // case of the small, long-sequence groups of an evaluator payload.
+  if (group && a.mode == BIAS_COORDS && attn_pad16(a.S) > 80) {
+    const int per_sm = attn_smem_bytes(a.S, dp, group, a.table_rows) <= 113 * 1024 ? 2 : 1;
+    if (a.B < per_sm * num_sms()) group = 0;
+  }
   if (group) {
     a.group = group;
     const int smem = attn_smem_bytes(a.S, dp, group, a.table_rows);
