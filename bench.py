@@ -746,6 +746,7 @@ def run_serve(args, name, cfg, rank, world, local, device):
 
     req = ev.stage_payload(payload)
     groups = req["groups"]
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
     offsets = np.asarray(payload["node_row_offsets"], dtype=np.int64)
     b = req["b"]
 
@@ -806,8 +807,9 @@ def run_serve(args, name, cfg, rank, world, local, device):
                     "note": "ShrimpEvaluator.evaluate_payload per step: host staging, plan_groups, one H2D, the "
                             "group forwards, one D2H and the reply bytes"},
             # per group the whole forward: prep_csr, tokens, stem, the trunk, policy conv, heads
-            "gpu_launches": len(groups) * ShrimpNet.kernel_launches(cfg["trunk_layout"], grid=False,
-                                                                    channels=cfg["channels"]) * args.steps,
+            "gpu_launches": sum(ShrimpNet.kernel_launches(cfg["trunk_layout"], grid=False, channels=cfg["channels"],
+                                                          pooled=ShrimpNet.pools_cells_apart(e - s, pad, sms))
+                                for s, e, pad in groups) * args.steps,
             "groups": len(groups),
             "nodes": {"min": int(sizes.min()), "p50": int(np.median(sizes)), "max": int(sizes.max())},
             "clocks": clocks,

@@ -587,8 +587,14 @@ constexpr size_t hex_conv_workspace_for(size_t rows) {
 struct FwdLayout {
   size_t seq32, xa16, y16, qkv16, o16, u16, feat16, gidx, rowmask, coords32, seqlen, slotcell, gflag;
   size_t pol32, vlog, mllog;  // payload path only: policy and head logits of a group
+  size_t pool, poolc;         // cell-mean unit sums (pool_cells_apart batches only)
   size_t total;
 };
+
+// Batches whose heads_kernel grid (four positions per CTA) is less than one
+// CTA per SM, with more than one pooling chunk of cells, pool the cell mean
+// in pool_cells_kernel first: one warp per (position, chunk, parity) unit.
+bool pool_cells_apart(int B, int npad) { return cdiv(B, 4) < num_sms() && pool_chunks(npad) > 1; }
 
 FwdLayout fwd_layout(int C, int B, int npad, bool payload) {
   const size_t S = (size_t)npad + kNumTok;
@@ -619,6 +625,11 @@ FwdLayout fwd_layout(int C, int B, int npad, bool payload) {
     L.pol32 = take(Mc * 4);
     L.vlog = take((size_t)B * kBins * 4);
     L.mllog = take((size_t)B * kBins * 4);
+  }
+  if (pool_cells_apart(B, npad)) {
+    const size_t units = (size_t)B * pool_chunks(npad) * 2;
+    L.pool = take(units * C * 4);
+    L.poolc = take(units * 4);
   }
   L.total = off;
   return L;
@@ -877,6 +888,15 @@ int forward_body(const sb_net* net, int B, int npad, const FwdLayout& L, uint8_t
     if (io.priors) {
       h.policy = io.policy; h.npad = npad; h.legal = io.legal; h.prior_offs = io.prior_offs;
       h.priors = io.priors; h.priors_logits = io.priors_logits;
+    }
+    if (pool_cells_apart(B, npad)) {
+      float* pool = reinterpret_cast<float*>(ws + L.pool);
+      float* pool_cnt = reinterpret_cast<float*>(ws + L.poolc);
+      const long long units = (long long)B * pool_chunks(npad) * 2;
+      launch_ex(pool_cells_kernel, (unsigned)cdiv(units, kPoolThreads / 32), kPoolThreads, 0, st,
+                (const __half*)xa16, (const float*)rowmask, B, S, C, pool, pool_cnt);
+      if (int s = check_launch("pool_cells_kernel")) return s;
+      h.pool = pool; h.pool_cnt = pool_cnt;
     }
     // positions per CTA: 4, or 8 once four per CTA would take more than
     // two waves (fewer re-reads of the layer-1 weights). Larger groups (16,

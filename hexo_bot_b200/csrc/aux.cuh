@@ -285,7 +285,76 @@ struct HeadsArgs {
   const int64_t* prior_offs;  // (B) flat offsets
   float* priors;              // flat priors, or NULL (no reply)
   float* priors_logits;       // flat raw logits at the same offsets, or NULL
+  // cell-mean chunk sums from pool_cells_kernel ([B][chunks][2][C] and
+  // [B][chunks][2]), or NULL: the heads kernel pools the cells itself
+  const float* pool;
+  const float* pool_cnt;
 };
+
+// Masked cell mean (model.py:931-935) in a fixed order: a position's cell
+// rows are cut into chunks of kPoolRows, each chunk into its even and odd
+// rows; a (chunk, parity) unit adds its rows in row order, sixteen rows per
+// batch of loads, and the unit sums of one parity are added in chunk order.
+// The order depends only on the padded row count, so a position's mean is
+// the same whether heads_kernel pools in place or adds the unit sums that
+// pool_cells_kernel wrote, and whatever the rest of the batch is.
+constexpr int kPoolRows = 128;  // a multiple of 32: no load batch crosses a chunk
+constexpr int kPoolThreads = 128;
+__host__ __device__ constexpr int pool_chunks(int npad) { return (npad + kPoolRows - 1) / kPoolRows; }
+
+// Sum of rows n_begin, n_begin + 2, ... < n_end of one position (cell rows
+// from `base`), channels 4 c4 .. 4 c4 + 3, and the sum of their mask values.
+__device__ __forceinline__ float4 pool_unit(const __half* lnf16, const float* rowmask, long long base, int C, int c4,
+                                            int n_begin, int n_end, float& cnt) {
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  cnt = 0.f;
+  for (int n0 = n_begin; n0 < n_end; n0 += 32) {
+    uint2 v[16];  // four f16 channels
+    float mk[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const int n = n0 + 2 * q;
+      const bool in = n < n_end;
+      mk[q] = in ? __ldg(rowmask + base + n) : 0.f;
+      v[q] = in ? __ldg(reinterpret_cast<const uint2*>(lnf16 + (base + n) * C) + c4) : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v[q].x));
+      const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v[q].y));
+      s.x = fmaf(lo.x, mk[q], s.x);
+      s.y = fmaf(lo.y, mk[q], s.y);
+      s.z = fmaf(hi.x, mk[q], s.z);
+      s.w = fmaf(hi.y, mk[q], s.w);
+      cnt += mk[q];
+    }
+  }
+  return s;
+}
+
+// The unit sums for batches whose heads_kernel CTAs would leave most SMs
+// idle: one warp per (position, chunk, parity) unit, written to
+// pool[unit][C] and pool_cnt[unit], unit = (b * chunks + chunk) * 2 + parity.
+__global__ void __launch_bounds__(kPoolThreads) pool_cells_kernel(const __half* lnf16, const float* rowmask, int B,
+                                                                  int S, int C, float* pool, float* pool_cnt) {
+  pdl_launch_dependents();
+  pdl_wait();  // ln_final and the row mask come from earlier kernels
+  const int npad = S - kNumTok, nk = pool_chunks(npad);
+  const long long unit = (long long)blockIdx.x * (kPoolThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (unit >= (long long)B * nk * 2) return;
+  const int part = (int)(unit & 1);
+  const long long bk = unit >> 1;
+  const int b = (int)(bk / nk), k = (int)(bk - (long long)b * nk);
+  const long long base = (long long)b * S + kNumTok;
+  for (int c4 = lane; c4 < C / 4; c4 += 32) {
+    float cnt;
+    const float4 s = pool_unit(lnf16, rowmask, base, C, c4, k * kPoolRows + part, min(k * kPoolRows + kPoolRows, npad),
+                               cnt);
+    *reinterpret_cast<float4*>(pool + unit * C + 4 * c4) = s;
+    if (c4 == lane && lane == 0) pool_cnt[unit] = cnt;
+  }
+}
 
 constexpr int kHeadsThreads = 256;
 constexpr int kHeadsKC = 32;  // layer-1 weight rows per shared-memory chunk
@@ -324,7 +393,8 @@ __host__ __device__ constexpr int heads_smem_floats(int C, int P) {
 // one 16-byte load gives four positions. The kernel runs once per forward, at
 // MCTS batch sizes too, so it is built for latency: pooling gives each warp
 // half of one position's rows and loads them in batches of 16 before adding
-// them; the layer-1 weights stream through a ring of cp.async chunks (three
+// them (or adds the unit sums of pool_cells_kernel, when a small batch of
+// long positions ran it first); the layer-1 weights stream through a ring of cp.async chunks (three
 // in flight while one is used); the dot products are split over K across
 // thread groups and reduced in a fixed order.
 template <int P>
@@ -363,9 +433,9 @@ __device__ void heads_pass(const HeadsArgs& a, int pass, float* sm, int b0, int 
     vin[idx] = v;
   }
   if (pass == 0) {  // the cell mean is shared by both heads (kept in vin[2C, 3C))
-    // unit u = (position u / 2, rows of parity u % 2); the split does not
-    // depend on P, so a position's sum is the same in any batch
-    const int npad = S - kNumTok;
+    // unit u = (position u / 2, rows of parity u % 2), summed over the
+    // chunks in the order pool_unit documents
+    const int npad = S - kNumTok, nk = pool_chunks(npad);
     for (int u = warp; u < 2 * P; u += kHeadsThreads / 32) {
       const int p = u >> 1, part = u & 1;
       const bool live = p < npos;
@@ -373,27 +443,27 @@ __device__ void heads_pass(const HeadsArgs& a, int pass, float* sm, int b0, int 
       for (int c4 = lane; c4 < C / 4; c4 += 32) {
         float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
         float cnt = 0.f;
-        if (live) {
-          for (int n0 = part; n0 < npad; n0 += 32) {
-            uint2 v[16];  // four f16 channels
-            float mk[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const int n = n0 + 2 * q;
-              const bool in = n < npad;
-              mk[q] = in ? __ldg(a.rowmask + base + n) : 0.f;
-              v[q] = in ? __ldg(reinterpret_cast<const uint2*>(a.lnf16 + (base + n) * C) + c4) : make_uint2(0u, 0u);
-            }
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v[q].x));
-              const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v[q].y));
-              s.x = fmaf(lo.x, mk[q], s.x);
-              s.y = fmaf(lo.y, mk[q], s.y);
-              s.z = fmaf(hi.x, mk[q], s.z);
-              s.w = fmaf(hi.y, mk[q], s.w);
-              cnt += mk[q];
-            }
+        if (live && a.pool) {
+          const long long u0 = (long long)(b0 + p) * nk * 2 + part;
+#pragma unroll 4
+          for (int k = 0; k < nk; ++k) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(a.pool + (u0 + 2 * k) * C) + c4);
+            s.x += t.x;
+            s.y += t.y;
+            s.z += t.z;
+            s.w += t.w;
+            cnt += __ldg(a.pool_cnt + u0 + 2 * k);
+          }
+        } else if (live) {
+          for (int k = 0; k < nk; ++k) {
+            float ck;
+            const float4 t = pool_unit(a.lnf16, a.rowmask, base, C, c4, k * kPoolRows + part,
+                                       min(k * kPoolRows + kPoolRows, npad), ck);
+            s.x += t.x;
+            s.y += t.y;
+            s.z += t.z;
+            s.w += t.w;
+            cnt += ck;
           }
         }
         *reinterpret_cast<float4*>(red + u * C + 4 * c4) = s;

@@ -516,19 +516,30 @@ class ShrimpNet(nn.Module):
         )
 
     @staticmethod
-    def kernel_launches(layout: str, grid: bool = False, channels: int = 128) -> int:
+    def kernel_launches(layout: str, grid: bool = False, channels: int = 128, pooled: bool = False) -> int:
         """Kernels one forward_policy_value call enqueues. With `grid` (dense
         inputs of at most 81 cells, channels a multiple of 64 up to 128, at
         least 1024 positions) the geometry check runs and the first conv of
         every ConvBlock and the policy conv are launched twice, as the grid
         conv and as the windowed conv, one of which returns at once. An
         attention block is four launches (qkv, core, out_proj, the fused MLP)
-        at 64 or 128 channels and five (fc1 and fc2 apart) otherwise."""
+        at 64 or 128 channels and five (fc1 and fc2 apart) otherwise. With
+        `pooled` (see pools_cells_apart) the cell mean of the value heads is
+        one more launch."""
 
         n_conv = layout.count("C")
         dual = n_conv + 1 if grid else 0
         per_attn = 4 if channels in (64, 128) else 5
-        return 2 + (1 if grid else 0) + 1 + 2 * n_conv + 1 + dual + per_attn * layout.count("A") + 1
+        return (2 + (1 if grid else 0) + 1 + 2 * n_conv + 1 + dual + per_attn * layout.count("A") + 1
+                + (1 if pooled else 0))
+
+    @staticmethod
+    def pools_cells_apart(batch: int, npad: int, sms: int = 148) -> bool:
+        """The native rule for pooling the heads' cell mean in a kernel of its
+        own: fewer heads CTAs (four positions each) than SMs, and more than
+        one 128-row chunk of cells per position."""
+
+        return (batch + 3) // 4 < sms and (npad + 127) // 128 > 1
 
 
 __all__ = ["ShrimpNet", "HexNodeConv", "ConvBlock", "AttnBlock", "RelPosAttention", "LayerScale",

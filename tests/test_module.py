@@ -96,3 +96,8 @@ def test_kernel_launch_count():
     assert ShrimpNet.kernel_launches("CCACCACCACCA") == 2 + 1 + 16 + 16 + 2
     assert ShrimpNet.kernel_launches("CCACCACCACCA", channels=192) == 2 + 1 + 16 + 20 + 2
     assert ShrimpNet.kernel_launches("CCACCACCACCA", grid=True) == 2 + 1 + 1 + 16 + 9 + 16 + 2
+    # small batches of long positions pool the heads' cell mean in a kernel of their own
+    assert ShrimpNet.kernel_launches("CCACCACCACCA", pooled=True) == 2 + 1 + 16 + 16 + 2 + 1
+    assert ShrimpNet.pools_cells_apart(6, 2432) and ShrimpNet.pools_cells_apart(588, 129)
+    assert not ShrimpNet.pools_cells_apart(589, 129)  # 148 heads CTAs: one per SM
+    assert not ShrimpNet.pools_cells_apart(3, 128)  # one chunk of cells
