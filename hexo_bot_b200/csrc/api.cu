@@ -39,12 +39,11 @@ int fail(int code, const char* fmt, ...) {
 // SHRIMP_B200_SYNC_DEBUG=1: synchronise and log after every launch (debugging
 // aid; never set in serving).
 bool sync_debug() {
-  static int v = -1;
-  if (v < 0) {
+  static const bool v = [] {  // read once (thread-safe static initialisation)
     const char* e = getenv("SHRIMP_B200_SYNC_DEBUG");
-    v = (e && e[0] == '1') ? 1 : 0;
-  }
-  return v == 1;
+    return e && e[0] == '1';
+  }();
+  return v;
 }
 
 int check_launch(const char* what) {
@@ -72,12 +71,11 @@ inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 // forces it off / on for every batch.
 constexpr int kPdlMinBatch = 256;
 constexpr int kPdlMaxBatch = 1024;
-int pdl_setting() {  // -1 automatic, 0 off, 1 on
-  static int v = -2;
-  if (v == -2) {
+int pdl_setting() {  // -1 automatic, 0 off, 1 on; read once
+  static const int v = [] {
     const char* e = getenv("SHRIMP_B200_PDL");
-    v = (e && strcmp(e, "1") == 0) ? 1 : (e && strcmp(e, "0") == 0) ? 0 : -1;
-  }
+    return (e && strcmp(e, "1") == 0) ? 1 : (e && strcmp(e, "0") == 0) ? 0 : -1;
+  }();
   return v;
 }
 bool pdl_for_batch(int B) {
@@ -139,13 +137,17 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn encode_tiled() {
-  static EncodeTiledFn fn = nullptr;
+  // looked up until found; host threads racing on the first lookup store the same pointer
+  static std::atomic<EncodeTiledFn> cached{nullptr};
+  EncodeTiledFn fn = cached.load(std::memory_order_acquire);
   if (!fn) {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
+        q == cudaDriverEntryPointSuccess) {
       fn = reinterpret_cast<EncodeTiledFn>(p);
+      cached.store(fn, std::memory_order_release);
+    }
   }
   return fn;
 }
@@ -200,16 +202,18 @@ int make_tmap_3d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int es
 }
 
 int num_sms() {
-  static int cache[64] = {0};
+  // per device; host threads racing on a first query store the same value
+  static std::atomic<int> cache[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (!cache[dev]) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (!n) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 template <typename T>
